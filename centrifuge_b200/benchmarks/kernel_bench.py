@@ -1,0 +1,100 @@
+"""Kernel microbenchmarks: tcgen05 GEMM vs cuBLAS, attention fwd / filtered bwd.
+
+    python -m centrifuge_b200.benchmarks.kernel_bench [--json out.json]
+
+Times with CUDA events after warm-up; inputs larger than L2 for the GEMM shapes.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from centrifuge_b200.ops import fused, gemm
+
+
+def _time(fn, iters=20, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_gemm(shapes):
+    rows = []
+    for (M, N, K, a_mn, b_mn, name) in shapes:
+        A = torch.randn(K, M, device="cuda").bfloat16() if a_mn else torch.randn(M, K, device="cuda").bfloat16()
+        B = torch.randn(K, N, device="cuda").bfloat16() if b_mn else torch.randn(N, K, device="cuda").bfloat16()
+        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        ms = _time(lambda: gemm.gemm(A, B, out, a_mn, b_mn, gemm.EPI_BF16))
+        Am = A.t() if a_mn else A
+        Bm = B if b_mn else B.t()
+        ms_ref = _time(lambda: torch.matmul(Am, Bm))
+        fl = 2.0 * M * N * K
+        rows.append({"name": name, "M": M, "N": N, "K": K, "a_mn": a_mn, "b_mn": b_mn,
+                     "ms": ms, "tflops": fl / ms / 1e9, "cublas_ms": ms_ref,
+                     "cublas_tflops": fl / ms_ref / 1e9})
+        print(json.dumps(rows[-1]))
+    return rows
+
+
+def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3)):
+    ld = (nh + 2 * nkv) * hd
+    qkv = torch.randn(B * S, ld, device="cuda").bfloat16()
+    o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
+    ms_f = _time(lambda: fused.attn_fwd(qkv, B, S, nh, nkv, hd, out=o, lse=lse), iters=10)
+    fl_f = 4.0 * B * nh * hd * S * S / 2
+    res = [{"name": "attn_fwd", "ms": ms_f, "tflops": fl_f / ms_f / 1e9}]
+    print(json.dumps(res[-1]))
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for keep in keeps:
+        Sk = int(S * keep) // 8 * 8
+        pos = torch.stack([torch.randperm(S, device="cuda", generator=g)[:Sk].sort().values
+                           for _ in range(B)]).int()
+        flat = (pos + torch.arange(B, device="cuda", dtype=torch.int32).view(B, 1) * S).reshape(-1)
+        qkv_k = qkv[flat.long()].contiguous()
+        o_k = o[flat.long()].contiguous()
+        lse_k = lse[flat.long()].contiguous()
+        do_k = torch.randn(B * Sk, nh * hd, device="cuda").bfloat16()
+        dq = torch.empty_like(qkv_k)
+        ms = _time(lambda: fused.attn_bwd(qkv_k, qkv, o_k, do_k, lse_k, pos, B, S, Sk, nh, nkv, hd,
+                                          dqkv_k=dq), iters=10)
+        # useful flops: dK/dV part over kept x kept (causal) + dQ part over kept x all keys
+        fl = 4.0 * B * nh * hd * (Sk * Sk / 2) + 6.0 * B * nh * hd * (Sk * S / 2)
+        res.append({"name": f"attn_bwd_keep{keep}", "Sk": Sk, "ms": ms, "tflops": fl / ms / 1e9})
+        print(json.dumps(res[-1]))
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--json", default=None)
+    ap.add_argument("--skip-attn", action="store_true")
+    args = ap.parse_args()
+    shapes = [
+        (8192, 8192, 8192, False, False, "square"),
+        (16384, 2560, 2048, False, False, "tinyllama_qkv_fwd"),
+        (16384, 11264, 2048, False, False, "tinyllama_gateup_fwd"),
+        (16384, 2048, 5632, False, False, "tinyllama_down_fwd"),
+        (8192, 2048, 5632, False, True, "tinyllama_down_dgrad_kept"),
+        (2048, 5632, 8192, True, True, "tinyllama_down_wgrad_kept"),
+        (16384, 32000, 2048, False, False, "tinyllama_lmhead_fwd"),
+    ]
+    out = {"gemm": bench_gemm(shapes)}
+    if not args.skip_attn:
+        out["attention"] = bench_attention()
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(out, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,377 @@
+// Python bindings of the sm_100a kernels (module centrifuge_b200._kernels).
+//
+// Each binding checks devices, dtypes, shapes and strides of its tensors, then launches the
+// kernel on the current CUDA stream.  A non-zero launcher status raises a RuntimeError: there is
+// no fallback path on the GPU.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "kernels/launch_api.h"
+
+namespace {
+
+using at::Tensor;
+
+#define CFB_CHECK_RC(rc, what) TORCH_CHECK((rc) == 0, what, " failed with status ", (rc))
+
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+inline void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+inline void check_bf16_2d(const Tensor& t, const char* name) {
+  check_cuda(t, name);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+}
+template <typename T>
+inline const T* opt_ptr(const c10::optional<Tensor>& t) {
+  return (t.has_value() && t->defined()) ? static_cast<const T*>(t->data_ptr()) : nullptr;
+}
+
+Tensor& err_word(int device) {
+  static std::vector<Tensor> words(64);
+  Tensor& w = words.at(device);
+  if (!w.defined())
+    w = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+  return w;
+}
+
+// out[M, N] = epi(alpha * op(a) @ op(b))
+//   a: [M, K] (a_mn = false) or [K, M] (a_mn = true)
+//   b: [N, K] (b_mn = false) or [K, N] (b_mn = true)
+void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, int64_t epi,
+          const c10::optional<Tensor>& resid, double alpha, int64_t bn, int64_t max_ctas) {
+  check_bf16_2d(a, "a");
+  check_bf16_2d(b, "b");
+  check_cuda(out, "out");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "out must be 2-D row-major");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm: inner dimensions differ (", K, " vs ", Kb, ")");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm: out has shape ", out.sizes(),
+              ", expected [", M, ", ", N, "]");
+  if (epi == kEpiBF16 || epi == kEpiBF16Resid) {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16, "gemm: bf16 epilogue needs a bf16 out");
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "gemm: fp32 epilogue needs an fp32 out");
+  }
+  const void* r = nullptr;
+  int64_t ldr = 0;
+  if (epi == kEpiBF16Resid) {
+    TORCH_CHECK(resid.has_value() && resid->defined(), "gemm: residual epilogue needs resid");
+    check_bf16_2d(*resid, "resid");
+    TORCH_CHECK(resid->size(0) == M && resid->size(1) == N, "gemm: resid shape mismatch");
+    r = resid->data_ptr();
+    ldr = resid->stride(0);
+  }
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  if (K == 0) {
+    if (epi != kEpiF32Acc && epi != kEpiBF16Resid) out.zero_();
+    if (epi == kEpiBF16Resid) out.copy_(*resid);
+    return;
+  }
+  int rc = cfb_gemm_bf16(a.data_ptr(), a.stride(0), a_mn, b.data_ptr(), b.stride(0), b_mn,
+                         out.data_ptr(), out.stride(0), static_cast<int>(epi), r, ldr,
+                         static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                         static_cast<float>(alpha),
+                         err_word(a.get_device()).data_ptr<int>(), static_cast<int>(bn),
+                         static_cast<int>(max_ctas), cur_stream());
+  CFB_CHECK_RC(rc, "gemm");
+}
+
+int64_t gemm_error_word(int64_t device, bool reset) {
+  Tensor& w = err_word(static_cast<int>(device));
+  const int64_t v = w.item<int>();
+  if (reset) w.zero_();
+  return v;
+}
+
+void rmsnorm_fwd(const Tensor& x, const Tensor& w, Tensor& y, const c10::optional<Tensor>& rstd,
+                 double eps) {
+  check_bf16_2d(x, "x");
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && w.is_contiguous(), "rmsnorm: contiguous");
+  const int rows = x.size(0), H = x.size(1);
+  float* rp = nullptr;
+  if (rstd.has_value() && rstd->defined()) {
+    TORCH_CHECK(rstd->scalar_type() == at::kFloat && rstd->numel() >= rows, "rstd");
+    rp = rstd->data_ptr<float>();
+  }
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rp, rows, H,
+                               static_cast<float>(eps), cur_stream()),
+               "rmsnorm_fwd");
+}
+
+void rmsnorm_bwd(const Tensor& dy, const Tensor& x, const c10::optional<Tensor>& x_rows,
+                 const Tensor& rstd, const Tensor& w, const c10::optional<Tensor>& dres,
+                 Tensor& dx, Tensor& dw_acc, int64_t partial_rows) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(x, "x");
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous(), "contiguous");
+  TORCH_CHECK(dw_acc.scalar_type() == at::kFloat && dw_acc.is_contiguous(), "dw_acc fp32");
+  const int rows = dy.size(0), H = dy.size(1);
+  if (rows == 0) return;
+  if (x_rows.has_value() && x_rows->defined())
+    TORCH_CHECK(x_rows->scalar_type() == at::kInt && x_rows->numel() == rows, "x_rows int32");
+  int P = static_cast<int>(std::min<int64_t>(partial_rows, rows));
+  if (P < 1) P = 1;
+  const c10::cuda::CUDAGuard guard(dy.device());
+  Tensor partial = at::empty({P, H}, dy.options().dtype(at::kFloat));
+  CFB_CHECK_RC(cfb_rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), opt_ptr<int>(x_rows),
+                               rstd.data_ptr<float>(), w.data_ptr(), opt_ptr<void>(dres),
+                               dx.data_ptr(), partial.data_ptr<float>(), dw_acc.data_ptr<float>(),
+                               rows, H, P, cur_stream()),
+               "rmsnorm_bwd");
+}
+
+void rope(Tensor& qkv, const Tensor& pos, int64_t n_heads, int64_t head_dim,
+          const Tensor& cos_sin, bool inverse) {
+  check_bf16_2d(qkv, "qkv");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.numel() == qkv.size(0), "pos int32 [rows]");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos_sin fp32");
+  TORCH_CHECK(n_heads * head_dim <= qkv.size(1), "rope: heads exceed the row");
+  if (qkv.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  CFB_CHECK_RC(cfb_rope(qkv.data_ptr(), qkv.stride(0), pos.data_ptr<int>(), nullptr, qkv.size(0),
+                        n_heads, head_dim, cos_sin.data_ptr<float>(), inverse ? 1 : 0,
+                        cur_stream()),
+               "rope");
+}
+
+void swiglu_fwd(const Tensor& gu, Tensor& h) {
+  TORCH_CHECK(gu.is_contiguous() && h.is_contiguous(), "swiglu: contiguous");
+  const int rows = gu.size(0), F = h.size(1);
+  TORCH_CHECK(gu.size(1) == 2 * F, "swiglu: gu must be [rows, 2F]");
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard guard(gu.device());
+  CFB_CHECK_RC(cfb_swiglu_fwd(gu.data_ptr(), h.data_ptr(), rows, F, cur_stream()), "swiglu_fwd");
+}
+
+void swiglu_bwd(const Tensor& dh, const Tensor& gu, const c10::optional<Tensor>& gu_rows,
+                Tensor& dgu) {
+  TORCH_CHECK(dh.is_contiguous() && gu.is_contiguous() && dgu.is_contiguous(), "contiguous");
+  const int rows = dh.size(0), F = dh.size(1);
+  TORCH_CHECK(dgu.size(0) == rows && dgu.size(1) == 2 * F, "dgu shape");
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard guard(dh.device());
+  CFB_CHECK_RC(cfb_swiglu_bwd(dh.data_ptr(), gu.data_ptr(), opt_ptr<int>(gu_rows), dgu.data_ptr(),
+                              rows, F, cur_stream()),
+               "swiglu_bwd");
+}
+
+void gather_rows(const Tensor& src, const Tensor& idx, Tensor& dst) {
+  check_cuda(src, "src");
+  TORCH_CHECK(src.dim() == 2 && src.stride(1) == 1 && dst.dim() == 2 && dst.stride(1) == 1,
+              "gather_rows: 2-D row-major");
+  TORCH_CHECK(idx.scalar_type() == at::kInt && idx.numel() == dst.size(0), "idx int32 [rows]");
+  TORCH_CHECK(src.size(1) == dst.size(1) && src.scalar_type() == dst.scalar_type(), "gather dims");
+  const int64_t es = src.element_size();
+  if (dst.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(src.device());
+  CFB_CHECK_RC(cfb_gather_rows(src.data_ptr(), src.stride(0) * es, idx.data_ptr<int>(),
+                               dst.data_ptr(), dst.stride(0) * es, dst.size(0),
+                               static_cast<int>(dst.size(1) * es), cur_stream()),
+               "gather_rows");
+}
+
+void embedding_fwd(const Tensor& table, const Tensor& ids, Tensor& out) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "ids int64");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous(), "contiguous");
+  if (ids.numel() == 0) return;
+  const c10::cuda::CUDAGuard guard(table.device());
+  CFB_CHECK_RC(cfb_embedding_fwd(table.data_ptr(), reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()), out.data_ptr(),
+                                 ids.numel(), table.size(1), cur_stream()),
+               "embedding_fwd");
+}
+
+void embedding_bwd(const Tensor& dy, const Tensor& ids, const c10::optional<Tensor>& id_rows,
+                   Tensor& dtable) {
+  TORCH_CHECK(dtable.scalar_type() == at::kFloat && dtable.is_contiguous(), "dtable fp32");
+  TORCH_CHECK(dy.is_contiguous() && ids.scalar_type() == at::kLong, "dy/ids");
+  if (dy.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(dy.device());
+  CFB_CHECK_RC(cfb_embedding_bwd(dy.data_ptr(), reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()),
+                                 reinterpret_cast<const int*>(opt_ptr<int>(id_rows)),
+                                 dtable.data_ptr<float>(), dy.size(0), dy.size(1), cur_stream()),
+               "embedding_bwd");
+}
+
+void ce_fwd(const Tensor& logits, const Tensor& labels, Tensor& loss, Tensor& lse) {
+  check_bf16_2d(logits, "logits");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.numel() == logits.size(0), "labels");
+  TORCH_CHECK(loss.scalar_type() == at::kFloat && lse.scalar_type() == at::kFloat, "fp32 outs");
+  if (logits.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  CFB_CHECK_RC(cfb_ce_fwd(logits.data_ptr(), logits.stride(0), reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                          loss.data_ptr<float>(), lse.data_ptr<float>(), logits.size(0),
+                          logits.size(1), cur_stream()),
+               "ce_fwd");
+}
+
+void ce_bwd(const Tensor& logits, const c10::optional<Tensor>& rows, const Tensor& labels,
+            const Tensor& lse, const Tensor& dloss, Tensor& dlogits) {
+  check_bf16_2d(logits, "logits");
+  check_bf16_2d(dlogits, "dlogits");
+  TORCH_CHECK(dloss.scalar_type() == at::kFloat && dloss.numel() == dlogits.size(0), "dloss");
+  if (dlogits.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  CFB_CHECK_RC(cfb_ce_bwd(logits.data_ptr(), logits.stride(0), opt_ptr<int>(rows),
+                          reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()), lse.data_ptr<float>(),
+                          dloss.data_ptr<float>(), dlogits.data_ptr(), dlogits.stride(0),
+                          dlogits.size(0), logits.size(1), cur_stream()),
+               "ce_bwd");
+}
+
+void adamw(Tensor& master, const Tensor& grad, Tensor& m, Tensor& v, Tensor& param, double lr,
+           double b1, double b2, double eps, double wd, double bc1, double bc2,
+           const c10::optional<Tensor>& grad_scale) {
+  TORCH_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat, "fp32");
+  TORCH_CHECK(param.scalar_type() == at::kBFloat16, "param bf16");
+  const int64_t n = master.numel();
+  TORCH_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n && param.numel() == n, "n");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(master.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(grad.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(m.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(v.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(param.data_ptr()) & 7) == 0,
+              "adamw: buffers must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(master.device());
+  CFB_CHECK_RC(cfb_adamw(master.data_ptr<float>(), grad.data_ptr<float>(), m.data_ptr<float>(),
+                         v.data_ptr<float>(), param.data_ptr(), n, lr, b1, b2, eps, wd, bc1, bc2,
+                         opt_ptr<float>(grad_scale), cur_stream()),
+               "adamw");
+}
+
+void sumsq(const Tensor& x, Tensor& partial) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && partial.scalar_type() == at::kFloat, "fp32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_sumsq(x.data_ptr<float>(), x.numel(), partial.data_ptr<float>(),
+                         static_cast<int>(partial.numel()), cur_stream()),
+               "sumsq");
+}
+
+void clip_coef(const Tensor& partials, double max_norm, double extra_scale, Tensor& coef,
+               Tensor& norm) {
+  const c10::cuda::CUDAGuard guard(partials.device());
+  CFB_CHECK_RC(cfb_clip_coef(partials.data_ptr<float>(), partials.numel(), max_norm, extra_scale,
+                             coef.data_ptr<float>(), norm.data_ptr<float>(), cur_stream()),
+               "clip_coef");
+}
+
+void drop_smallest(const Tensor& score, Tensor& mask, int64_t start, int64_t end, int64_t k) {
+  TORCH_CHECK(score.scalar_type() == at::kFloat && score.dim() == 2 && score.stride(1) == 1,
+              "score fp32 2-D");
+  TORCH_CHECK(mask.dim() == 2 && mask.stride(1) == 1 && mask.size(0) == score.size(0), "mask");
+  TORCH_CHECK(end <= score.size(1) && end <= mask.size(1), "drop_smallest: range");
+  int* m32 = nullptr;
+  long long* m64 = nullptr;
+  if (mask.scalar_type() == at::kLong)
+    m64 = reinterpret_cast<long long*>(mask.data_ptr<int64_t>());
+  else if (mask.scalar_type() == at::kInt)
+    m32 = mask.data_ptr<int>();
+  else
+    TORCH_CHECK(false, "mask must be int32 or int64");
+  if (score.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(score.device());
+  CFB_CHECK_RC(cfb_drop_smallest(score.data_ptr<float>(), score.stride(0), m32, m64,
+                                 mask.stride(0), score.size(0), start, end, k, cur_stream()),
+               "drop_smallest");
+}
+
+void keep_index(const Tensor& mask, int64_t S_keep, Tensor& pos, Tensor& flat_rows, Tensor& err) {
+  TORCH_CHECK(mask.scalar_type() == at::kLong && mask.is_contiguous() && mask.dim() == 2,
+              "mask int64 [B, S]");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && flat_rows.scalar_type() == at::kInt, "int32");
+  const c10::cuda::CUDAGuard guard(mask.device());
+  CFB_CHECK_RC(cfb_keep_index(reinterpret_cast<const long long*>(mask.data_ptr<int64_t>()),
+                              mask.size(0), mask.size(1), S_keep, pos.data_ptr<int>(),
+                              flat_rows.data_ptr<int>(), err.data_ptr<int>(), cur_stream()),
+               "keep_index");
+}
+
+void cast_f32_bf16(const Tensor& x, Tensor& y) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_cast_f32_bf16(x.data_ptr<float>(), y.data_ptr(), x.numel(), cur_stream()),
+               "cast");
+}
+
+void scale_f32(Tensor& x, double s) {
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_scale_f32(x.data_ptr<float>(), x.numel(), s, cur_stream()), "scale");
+}
+
+void attn_fwd(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S, int64_t nh,
+              int64_t nkv, int64_t hd, double scale) {
+  check_bf16_2d(qkv, "qkv");
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(qkv.size(0) == B * S && out.size(0) == B * S, "attn_fwd: rows");
+  TORCH_CHECK(qkv.size(1) >= (nh + 2 * nkv) * hd && out.size(1) >= nh * hd, "attn_fwd: cols");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * S * nh, "lse [T, nh] fp32");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  CFB_CHECK_RC(cfb_attn_fwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0),
+                            lse.data_ptr<float>(), B, S, nh, nkv, hd, scale, cur_stream()),
+               "attn_fwd");
+}
+
+void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, const Tensor& do_k,
+              const Tensor& lse_k, const Tensor& pos_k, Tensor& dqkv_k, Tensor& delta, int64_t B,
+              int64_t S, int64_t Sk, int64_t nh, int64_t nkv, int64_t hd, double scale) {
+  check_bf16_2d(qkv_k, "qkv_k");
+  check_bf16_2d(qkv_full, "qkv_full");
+  check_bf16_2d(o_k, "o_k");
+  check_bf16_2d(do_k, "do_k");
+  check_bf16_2d(dqkv_k, "dqkv_k");
+  TORCH_CHECK(qkv_k.stride(0) == qkv_full.stride(0) && dqkv_k.stride(0) == qkv_k.stride(0),
+              "attn_bwd: qkv buffers share the row stride");
+  TORCH_CHECK(o_k.stride(0) == do_k.stride(0), "attn_bwd: o and do share the row stride");
+  TORCH_CHECK(qkv_k.size(0) == B * Sk && qkv_full.size(0) == B * S, "attn_bwd: rows");
+  TORCH_CHECK(pos_k.scalar_type() == at::kInt && pos_k.numel() == B * Sk, "pos_k int32");
+  TORCH_CHECK(delta.scalar_type() == at::kFloat && delta.numel() >= B * Sk * nh, "delta");
+  TORCH_CHECK(lse_k.scalar_type() == at::kFloat && lse_k.numel() == B * Sk * nh, "lse_k");
+  const c10::cuda::CUDAGuard guard(qkv_k.device());
+  CFB_CHECK_RC(cfb_attn_bwd(qkv_k.data_ptr(), qkv_k.stride(0), qkv_full.data_ptr(),
+                            o_k.data_ptr(), o_k.stride(0), do_k.data_ptr(),
+                            lse_k.data_ptr<float>(), pos_k.data_ptr<int>(), dqkv_k.data_ptr(),
+                            nullptr, delta.data_ptr<float>(), B, S, Sk, nh, nkv, hd, scale,
+                            cur_stream()),
+               "attn_bwd");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of centrifuge_b200";
+  m.def("gemm", &gemm, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("out"),
+        py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("resid") = py::none(),
+        py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
+  m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("gather_rows", &gather_rows);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("adamw", &adamw);
+  m.def("sumsq", &sumsq);
+  m.def("clip_coef", &clip_coef);
+  m.def("drop_smallest", &drop_smallest);
+  m.def("keep_index", &keep_index);
+  m.def("cast_f32_bf16", &cast_f32_bf16);
+  m.def("scale_f32", &scale_f32);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+  m.attr("EPI_BF16") = static_cast<int>(kEpiBF16);
+  m.attr("EPI_BF16_RESID") = static_cast<int>(kEpiBF16Resid);
+  m.attr("EPI_F32") = static_cast<int>(kEpiF32);
+  m.attr("EPI_F32_ACC") = static_cast<int>(kEpiF32Acc);
+}

@@ -1,0 +1,407 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation tensor cores.
+//
+//   D[M, N] = epilogue( alpha * sum_k A[m, k] * B[k, n] )
+//
+// A is given either K-major (row-major [M, K]) or MN-major (row-major [K, M]); B either
+// K-major (row-major [N, K]) or MN-major (row-major [K, N]).  This covers the three GEMMs of a
+// linear layer without any transposes:
+//   forward   Y  = X  W^T     A = X  [T, K] K-major,   B = W [N, K]  K-major
+//   dgrad     dX = dY W       A = dY [T, N] K-major,   B = W [N, K]  MN-major
+//   wgrad     dW = dY^T X     A = dY [T, N] MN-major,  B = X [T, K]  MN-major
+//
+// Roles (192 threads, one CTA per SM, grid = min(#tiles, #SMs)):
+//   warp 0  TMA producer: 128B-swizzled tiles of A and B into a STAGES-deep smem ring
+//   warp 1  MMA issuer:   tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators
+//   warps 2-5 epilogue:   tcgen05.ld of the accumulator, fused epilogue, global stores
+// The two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i overlap the
+// MMAs of tile i+1.  Every mbarrier wait is bounded (see sm100_common.cuh); on timeout the
+// kernel records an error code, drains its own in-flight work and frees TMEM.
+#include "sm100_common.cuh"
+#include "launch_api.h"
+
+#include <cudaTypedefs.h>
+#include <mutex>
+
+namespace cfb {
+
+struct GemmArgs {
+  int M, N, K;
+  void* D;
+  long long ldd;
+  const __nv_bfloat16* R;
+  long long ldr;
+  float alpha;
+  int* err;
+};
+
+template <int BN>
+struct GemmShape {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& tm, int& tn) {
+  constexpr int GROUP = 16;
+  const int per_group = GROUP * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * GROUP;
+  const int gsize = min(num_m - first_m, GROUP);
+  const int r = tile - g * per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA,
+                    const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+  using S = GemmShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* bar_area = smem + S::STAGES * S::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty = full + S::STAGES;
+  uint64_t* tfull = empty + S::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int num_m = (p.M + S::BM - 1) / S::BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + S::BK - 1) / S::BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 4);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      int last_stage = -1;
+      uint32_t last_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, num_m, num_n, tm, tn);
+        const int m0 = tm * S::BM, n0 = tn * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err,
+                         kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_arrive_expect_tx(fb, S::STAGE_BYTES);
+          const uint32_t sa = smem_base + stage * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+          const int k0 = kb * S::BK;
+          if (!A_MN) {
+            tma_load_2d(sa, &tmA, fb, k0, m0);
+          } else {
+            tma_load_2d(sa, &tmA, fb, m0, k0);
+            tma_load_2d(sa + 8192, &tmA, fb, m0 + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(sb, &tmB, fb, k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &tmB, fb, n0 + c * 64, k0);
+          }
+          last_stage = stage;
+          last_phase = phase;
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && last_stage >= 0) {
+        // Let our own last copies land before the CTA exits (bounded).
+        volatile int dummy = 0;
+        mbar_wait(smem_u32(&full[last_stage]), last_phase, &dummy, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t IDESC = idesc_bf16_f32(128, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < S::BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(sa + k * 2048, 8192, 1024)
+                                     : sdesc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024)
+                                     : sdesc_sw128(sb + k * 32, 16, 1024);
+            umma_bf16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&empty[stage]));
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&tfull[acc]));
+      }
+      // All issued MMAs complete before TMEM is released.
+      umma_commit(smem_u32(drain));
+      volatile int dummy = 0;
+      mbar_wait(smem_u32(drain), 0, &dummy, nullptr, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(tile, num_m, num_n, tm, tn);
+      const int m0 = tm * S::BM, n0 = tn * BN;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err, kErrWaitEpilogue))
+        break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col = n0 + c * 32;
+        if (col >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        CFB_TMEM_LD32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (row < p.M) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+          if (EPI == kEpiBF16 || EPI == kEpiBF16Resid) {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+            if (EPI == kEpiBF16Resid) {
+              const uint4* rs = reinterpret_cast<const uint4*>(p.R + row * p.ldr + col);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                uint4 u = rs[j];
+                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float2 f = __bfloat1622float2(h[e]);
+                  v[j * 8 + 2 * e] += f.x;
+                  v[j * 8 + 2 * e + 1] += f.y;
+                }
+              }
+            }
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 u;
+              u.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
+              u.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
+              u.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
+              u.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
+              d4[j] = u;
+            }
+          } else {
+            float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col;
+            float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              if (EPI == kEpiF32Acc) {
+                const float4 old = d4[j];
+                o.x += old.x;
+                o.y += old.y;
+                o.z += old.z;
+                o.w += old.w;
+              }
+              d4[j] = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, S::TMEM_COLS);
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult qres;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix of `rows` x `cols` with leading dimension `ld`
+// (elements); boxes of `box_cols` x `box_rows` with 128-byte swizzle.
+int make_tmap_2d_bf16(CUtensorMap* map, const void* ptr, long long rows, long long cols,
+                      long long ld, int box_cols, int box_rows) {
+  auto fn = get_encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                       cudaStream_t st, int max_ctas) {
+  using S = GemmShape<BN>;
+  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+    configured = true;
+  }
+  const int tiles = ((a.M + 127) / 128) * ((a.N + BN - 1) / BN);
+  int grid = tiles < num_sms() ? tiles : num_sms();
+  if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+  kern<<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+template <int BN, int EPI>
+static int dispatch_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                          const GemmArgs& a, cudaStream_t st, int max_ctas) {
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false, EPI>(ta, tb, a, st, max_ctas);
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true, EPI>(ta, tb, a, st, max_ctas);
+  if (a_mn && b_mn) return launch_gemm<BN, true, true, EPI>(ta, tb, a, st, max_ctas);
+  return launch_gemm<BN, true, false, EPI>(ta, tb, a, st, max_ctas);
+}
+
+template <int BN>
+static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
+                        const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st, int max_ctas) {
+  switch (epi) {
+    case kEpiBF16: return dispatch_major<BN, kEpiBF16>(a_mn, b_mn, ta, tb, a, st, max_ctas);
+    case kEpiBF16Resid:
+      return dispatch_major<BN, kEpiBF16Resid>(a_mn, b_mn, ta, tb, a, st, max_ctas);
+    case kEpiF32: return dispatch_major<BN, kEpiF32>(a_mn, b_mn, ta, tb, a, st, max_ctas);
+    case kEpiF32Acc: return dispatch_major<BN, kEpiF32Acc>(a_mn, b_mn, ta, tb, a, st, max_ctas);
+  }
+  return -4;
+}
+
+}  // namespace cfb
+
+using namespace cfb;
+
+int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                  void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
+                  int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0) return -10;
+  if ((N % 32) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -11;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (reinterpret_cast<uintptr_t>(D) & 15))
+    return -12;
+  if (bn != 128 && bn != 256) {
+    const long long tiles256 = ((M + 127LL) / 128) * ((N + 255LL) / 256);
+    bn = (N <= 128 || tiles256 < num_sms()) ? 128 : 256;
+  }
+  CUtensorMap ta, tb;
+  int rc;
+  // A: K-major [M, K] (ld=lda) or MN-major [K, M]
+  rc = a_mn ? make_tmap_2d_bf16(&ta, A, K, M, lda, 64, 64)
+            : make_tmap_2d_bf16(&ta, A, M, K, lda, 64, 128);
+  if (rc) return rc * 100 - 1;
+  rc = b_mn ? make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, 64)
+            : make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, bn);
+  if (rc) return rc * 100 - 2;
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.D = D;
+  a.ldd = ldd;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.ldr = ldr;
+  a.alpha = alpha;
+  a.err = err;
+  if (bn == 256) return dispatch_epi<256>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
+  return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
+}

@@ -1,0 +1,58 @@
+// Host-side launchers of the sm_100a kernels.  Plain C++ entry points over raw device
+// pointers; the torch bindings (bindings.cpp) validate tensors and call these on the current
+// stream.  Every launcher returns 0 on success and a negative code on a bad argument or a
+// launch failure.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3 };
+
+// GEMM (gemm_sm100.cu): D = alpha * op(A) op(B) with the epilogue `epi`.
+int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                  void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
+                  int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st);
+
+// Row ops (fused_ops.cu).
+int cfb_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int H,
+                    float eps, cudaStream_t st);
+int cfb_rmsnorm_bwd(const void* dy, const void* x, const int* x_rows, const float* rstd,
+                    const void* w, const void* dres, void* dx, float* dw_partial, float* dw_acc,
+                    int rows, int H, int partial_rows, cudaStream_t st);
+int cfb_rope(void* qkv, long long ld, const int* pos, const int* row_of, int rows, int n_heads,
+             int head_dim, const float* cos_sin, int inverse, cudaStream_t st);
+int cfb_swiglu_fwd(const void* gu, void* h, int rows, int F, cudaStream_t st);
+int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu, int rows, int F,
+                   cudaStream_t st);
+int cfb_gather_rows(const void* src, long long ld_src, const int* idx, void* dst,
+                    long long ld_dst, int rows, int row_bytes, cudaStream_t st);
+int cfb_embedding_fwd(const void* table, const long long* ids, void* out, int rows, int H,
+                      cudaStream_t st);
+int cfb_embedding_bwd(const void* dy, const long long* ids, const int* id_rows, float* dtable,
+                      int rows, int H, cudaStream_t st);
+int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float* loss,
+               float* lse, int rows, int V, cudaStream_t st);
+int cfb_ce_bwd(const void* logits, long long ld, const int* logit_rows, const long long* labels,
+               const float* lse, const float* dloss, void* dlogits, long long ld_out, int rows,
+               int V, cudaStream_t st);
+int cfb_adamw(float* master, const float* grad, float* m, float* v, void* param_bf16, long long n,
+              float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2,
+              const float* grad_scale, cudaStream_t st);
+int cfb_sumsq(const float* x, long long n, float* out_partial, int nblocks, cudaStream_t st);
+int cfb_clip_coef(const float* partials, int n, float max_norm, float extra_scale, float* coef,
+                  float* norm_out, cudaStream_t st);
+int cfb_drop_smallest(const float* score, long long ld, int* mask_i32, long long* mask_i64,
+                      long long ld_mask, int rows, int start, int end, int k, cudaStream_t st);
+int cfb_keep_index(const long long* mask, int B, int S, int S_keep, int* pos, int* flat_rows,
+                   int* err, cudaStream_t st);
+int cfb_cast_f32_bf16(const float* x, void* y, long long n, cudaStream_t st);
+int cfb_scale_f32(float* x, long long n, float s, cudaStream_t st);
+
+// Attention (attention_fwd.cu / attention_bwd.cu).  Token-major layouts:
+//   q/k/v rows of the fused [T, ld] qkv buffer, heads at column offsets.
+int cfb_attn_fwd(const void* qkv, long long ld_qkv, void* out, long long ld_out, float* lse,
+                 int B, int S, int nh, int nkv, int hd, float scale, cudaStream_t st);
+int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, const void* o_k,
+                 long long ld_o, const void* do_k, const float* lse_k, const int* pos_k,
+                 void* dqkv_k, float* unused, float* delta, int B, int S, int Sk, int nh,
+                 int nkv, int hd, float scale, cudaStream_t st);

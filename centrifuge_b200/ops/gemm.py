@@ -1,0 +1,60 @@
+"""Linear-layer GEMMs on the tcgen05 kernel (csrc/kernels/gemm_sm100.cu).
+
+Shapes follow the PyTorch ``F.linear`` convention: ``x [T, K]``, ``w [N, K]``, ``y [T, N]``.
+
+* ``linear_fwd``     y  = x w^T            (both operands K-major)
+* ``linear_dgrad``   dx = dy w             (w read MN-major: no transpose copy)
+* ``linear_wgrad``   dW (+)= dy^T x        (both read MN-major; fp32 accumulate epilogue)
+
+CPU tensors run the fp32 reference (``torch.matmul``); CUDA tensors always run the kernel.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ._ext import kernels
+
+EPI_BF16, EPI_BF16_RESID, EPI_F32, EPI_F32_ACC = 0, 1, 2, 3
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, a_mn: bool, b_mn: bool,
+         epi: int = EPI_BF16, resid: Optional[torch.Tensor] = None, alpha: float = 1.0,
+         bn: int = 0, max_ctas: int = 0) -> torch.Tensor:
+    """``out = epi(alpha * op(a) @ op(b))`` with op(a) ``[M, K]`` and op(b) ``[K, N]``."""
+    if not a.is_cuda:
+        A = (a.t() if a_mn else a).float()
+        B = (b if b_mn else b.t()).float()
+        r = alpha * (A @ B)
+        if epi == EPI_BF16_RESID:
+            r = r + resid.float()
+        if epi == EPI_F32_ACC:
+            out += r
+        else:
+            out.copy_(r)
+        return out
+    kernels().gemm(a, b, out, a_mn, b_mn, epi, resid, alpha, bn, max_ctas)
+    return out
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+               resid: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    return gemm(x, w, out, False, False, EPI_BF16_RESID if resid is not None else EPI_BF16,
+                resid)
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 resid: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(dy.shape[0], w.shape[1], dtype=dy.dtype, device=dy.device)
+    return gemm(dy, w, out, False, True, EPI_BF16_RESID if resid is not None else EPI_BF16,
+                resid)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor,
+                 accumulate: bool = True, alpha: float = 1.0) -> torch.Tensor:
+    """``dw (+)= alpha * dy^T x``; ``dw`` is fp32 ``[N, K]`` (the flat gradient bucket)."""
+    return gemm(dy, x, dw, True, True, EPI_F32_ACC if accumulate else EPI_F32, None, alpha)

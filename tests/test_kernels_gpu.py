@@ -1,0 +1,219 @@
+"""sm_100a kernels against plain-PyTorch fp32 definitions of the same ops."""
+import math
+
+import pytest
+import torch
+
+from centrifuge_b200.ops import fused, gemm, reference as ref, select
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (304, 512, 200), (1024, 2560, 2048),
+                                   (80, 96, 136)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("bn", [128, 256])
+def test_gemm_layouts(M, N, K, a_mn, b_mn, bn):
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device=dev).bfloat16()
+    Bm = torch.randn(K, N, device=dev).bfloat16()
+    a = A.t().contiguous() if a_mn else A
+    b = Bm.contiguous() if b_mn else Bm.t().contiguous()
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    gemm.gemm(a, b, out, a_mn, b_mn, gemm.EPI_BF16, bn=bn)
+    torch.cuda.synchronize()
+    want = A.float() @ Bm.float()
+    assert rel_err(out, want) < 1e-2
+    from centrifuge_b200.ops import kernels
+    assert kernels().gemm_error_word(0, True) == 0
+
+
+def test_gemm_epilogues():
+    torch.manual_seed(1)
+    M, N, K = 512, 768, 384
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = torch.randn(N, K, device=dev).bfloat16()
+    r = torch.randn(M, N, device=dev).bfloat16()
+    y = gemm.linear_fwd(x, w, resid=r)
+    assert rel_err(y, x.float() @ w.float().t() + r.float()) < 1e-2
+    dy = torch.randn(M, N, device=dev).bfloat16()
+    dx = gemm.linear_dgrad(dy, w)
+    assert rel_err(dx, dy.float() @ w.float()) < 1e-2
+    dw = torch.ones(N, K, device=dev)
+    gemm.linear_wgrad(dy, x, dw, accumulate=True)
+    assert rel_err(dw, 1 + dy.float().t() @ x.float()) < 1e-2
+    gemm.linear_wgrad(dy, x, dw, accumulate=False, alpha=0.5)
+    assert rel_err(dw, 0.5 * dy.float().t() @ x.float()) < 1e-2
+
+
+def test_rmsnorm():
+    torch.manual_seed(2)
+    T, H = 300, 2048
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, device=dev)).bfloat16()
+    y, rstd = fused.rmsnorm_fwd(x, w, 1e-5)
+    yr, rr = ref.rmsnorm(x, w, 1e-5)
+    assert rel_err(y, yr) < 1e-2 and rel_err(rstd, rr) < 1e-4
+    rows = torch.randperm(T, device=dev)[:100].sort().values.int()
+    dy = torch.randn(100, H, device=dev).bfloat16()
+    dres = torch.randn(100, H, device=dev).bfloat16()
+    dw = torch.zeros(H, device=dev)
+    dx = fused.rmsnorm_bwd(dy, x, rstd, w, dw, x_rows=rows, dres=dres)
+    dxr, dwr = ref.rmsnorm_bwd(dy, x[rows.long()], rstd[rows.long()], w, dres)
+    assert rel_err(dx, dxr) < 1e-2 and rel_err(dw, dwr) < 1e-3
+
+
+def test_rope_roundtrip():
+    torch.manual_seed(3)
+    T, nh, nkv, hd = 64, 4, 2, 64
+    table = ref.rope_table(128, hd, 10000.0, dev)
+    qkv = torch.randn(T, (nh + 2 * nkv) * hd, device=dev).bfloat16()
+    pos = torch.randint(0, 128, (T,), device=dev, dtype=torch.int32)
+    want = ref.rope(qkv[:, : (nh + nkv) * hd].view(T, nh + nkv, hd), pos, table)
+    out = qkv.clone()
+    fused.rope_(out, pos, nh + nkv, hd, table)
+    assert rel_err(out[:, : (nh + nkv) * hd].view(T, nh + nkv, hd), want) < 1e-2
+    assert torch.equal(out[:, (nh + nkv) * hd:], qkv[:, (nh + nkv) * hd:])
+    fused.rope_(out, pos, nh + nkv, hd, table, inverse=True)
+    assert rel_err(out, qkv) < 2e-2
+
+
+def test_swiglu():
+    torch.manual_seed(4)
+    T, F = 100, 512
+    gu = torch.randn(T, 2 * F, device=dev).bfloat16()
+    h = fused.swiglu_fwd(gu)
+    assert rel_err(h, ref.swiglu(gu)) < 1e-2
+    rows = torch.arange(0, T, 3, device=dev, dtype=torch.int32)
+    dh = torch.randn(rows.numel(), F, device=dev).bfloat16()
+    dgu = fused.swiglu_bwd(dh, gu, rows)
+    assert rel_err(dgu, ref.swiglu_bwd(dh, gu[rows.long()])) < 1e-2
+
+
+def test_gather_embedding():
+    torch.manual_seed(5)
+    V, H, T = 1000, 256, 64
+    table = torch.randn(V, H, device=dev).bfloat16()
+    ids = torch.randint(0, V, (T,), device=dev)
+    e = fused.embedding_fwd(table, ids)
+    assert torch.equal(e, table[ids])
+    idx = torch.tensor([3, 5, 7, 63], device=dev, dtype=torch.int32)
+    g = fused.gather_rows(e, idx)
+    assert torch.equal(g, e[idx.long()])
+    dt = torch.zeros(V, H, device=dev)
+    dy = torch.randn(4, H, device=dev).bfloat16()
+    fused.embedding_bwd(dy, ids, dt, idx)
+    want = torch.zeros(V, H, device=dev).index_add_(0, ids[idx.long()], dy.float())
+    assert rel_err(dt, want) < 1e-5
+
+
+def test_cross_entropy():
+    torch.manual_seed(6)
+    T, V = 64, 32000
+    logits = (3 * torch.randn(T, V, device=dev)).bfloat16()
+    labels = torch.randint(0, V, (T,), device=dev)
+    labels[5] = -100
+    loss, lse = fused.ce_fwd(logits, labels)
+    lr, sr = ref.cross_entropy(logits, labels)
+    assert rel_err(loss, lr) < 1e-4 and rel_err(lse, sr) < 1e-5
+    rows = torch.tensor([0, 5, 9, 63], device=dev, dtype=torch.int32)
+    dloss = torch.rand(4, device=dev)
+    g = fused.ce_bwd(logits, labels, lse, dloss, rows)
+    want = ref.cross_entropy_bwd(logits[rows.long()], labels[rows.long()], sr[rows.long()], dloss)
+    assert rel_err(g, want) < 1e-2
+
+
+def test_adamw_matches_torch():
+    torch.manual_seed(7)
+    n = 10003
+    p = torch.randn(n, device=dev)
+    g = torch.randn(n, device=dev)
+    m = torch.zeros(n, device=dev)
+    v = torch.zeros(n, device=dev)
+    pb = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    tp = torch.nn.Parameter(p.clone())
+    opt = torch.optim.AdamW([tp], lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    for step in range(1, 4):
+        tp.grad = g.clone()
+        opt.step()
+        fused.adamw_(p, g, m, v, pb, 1e-3, 0.9, 0.95, 1e-8, 0.1, step)
+    assert rel_err(p, tp.detach()) < 1e-5
+    assert rel_err(pb, tp.detach()) < 1e-2
+
+
+def test_clip_coef():
+    g = torch.full((1000,), 2.0, device=dev)
+    coef = torch.empty(1, device=dev)
+    norm = torch.empty(1, device=dev)
+    fused.grad_norm_clip_coef(g, 1.0, 0.5, coef, norm)
+    n = math.sqrt(1000 * 4.0) * 0.5
+    assert abs(norm.item() - n) < 1e-3
+    assert abs(coef.item() - 0.5 / (n + 1e-6)) < 1e-6
+
+
+@pytest.mark.parametrize("S,drop", [(2048, 0.5), (224, 0.5), (4096, 0.3)])
+def test_drop_smallest_and_keep_index(S, drop):
+    from centrifuge_b200.loss import num_dropped
+    torch.manual_seed(8)
+    B = 3
+    score = torch.randn(B, S - 1, device=dev)
+    k = num_dropped(S, drop)
+    mask = torch.ones(B, S, dtype=torch.long, device=dev)
+    select.drop_smallest_(score, mask, k, 0, S - 1)
+    want = torch.ones(B, S, dtype=torch.long)
+    _, idx = torch.topk(score.cpu(), k, dim=1, largest=False)
+    want.scatter_(1, idx, 0)
+    assert torch.equal(mask.cpu(), want)
+    pos, flat, err = select.keep_index(mask, S - k)
+    assert err.item() == 0
+    pos_c, flat_c, _ = select.keep_index(want, S - k)
+    assert torch.equal(pos.cpu(), pos_c) and torch.equal(flat.cpu(), flat_c)
+
+
+@pytest.mark.parametrize("B,S,nh,nkv,hd", [(2, 256, 4, 2, 64), (1, 200, 4, 1, 128),
+                                           (2, 512, 8, 2, 128)])
+def test_attention_fwd(B, S, nh, nkv, hd):
+    torch.manual_seed(9)
+    ld = (nh + 2 * nkv) * hd
+    qkv = torch.randn(B * S, ld, device=dev).bfloat16()
+    o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
+    q = qkv[:, : nh * hd].reshape(B, S, nh, hd)
+    k = qkv[:, nh * hd:(nh + nkv) * hd].reshape(B, S, nkv, hd)
+    v = qkv[:, (nh + nkv) * hd:].reshape(B, S, nkv, hd)
+    orf, lr = ref.attention(q, k, v)
+    assert rel_err(o, orf.reshape(B * S, nh * hd)) < 1e-2
+    assert rel_err(lse, lr.reshape(B * S, nh)) < 1e-4
+
+
+@pytest.mark.parametrize("B,S,nh,nkv,hd,keep", [(2, 256, 4, 2, 64, 0.5), (1, 320, 4, 1, 128, 0.3),
+                                                (2, 256, 8, 2, 128, 1.0), (1, 128, 2, 2, 64, 0.7)])
+def test_attention_bwd_filtered(B, S, nh, nkv, hd, keep):
+    torch.manual_seed(10)
+    ld = (nh + 2 * nkv) * hd
+    qkv = (0.5 * torch.randn(B * S, ld, device=dev)).bfloat16()
+    o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
+    Sk = max(1, int(round(S * keep)))
+    pos = torch.stack([torch.cat([torch.randperm(S - 1, device=dev)[: Sk - 1].sort().values,
+                                  torch.tensor([S - 1], device=dev)]) for _ in range(B)])
+    pos = pos.sort(dim=1).values.int()
+    flat = (pos + torch.arange(B, device=dev, dtype=torch.int32).view(B, 1) * S).reshape(-1)
+    qkv_k = qkv[flat.long()].contiguous()
+    o_k = o[flat.long()].contiguous()
+    lse_k = lse[flat.long()].contiguous()
+    do_k = torch.randn(B * Sk, nh * hd, device=dev).bfloat16()
+    d = fused.attn_bwd(qkv_k, qkv, o_k, do_k, lse_k, pos, B, S, Sk, nh, nkv, hd)
+    q = qkv_k[:, : nh * hd].reshape(B, Sk, nh, hd)
+    kf = qkv[:, nh * hd:(nh + nkv) * hd].reshape(B, S, nkv, hd)
+    vf = qkv[:, (nh + nkv) * hd:].reshape(B, S, nkv, hd)
+    dq, dk, dv = ref.attention_bwd_filtered(q, kf, vf, o_k.reshape(B, Sk, nh, hd),
+                                            do_k.reshape(B, Sk, nh, hd), lse_k.reshape(B, Sk, nh),
+                                            pos)
+    assert rel_err(d[:, : nh * hd], dq.reshape(B * Sk, -1)) < 2e-2
+    assert rel_err(d[:, nh * hd:(nh + nkv) * hd], dk.reshape(B * Sk, -1)) < 2e-2
+    assert rel_err(d[:, (nh + nkv) * hd:], dv.reshape(B * Sk, -1)) < 2e-2
