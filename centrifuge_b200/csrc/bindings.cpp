@@ -343,7 +343,39 @@ void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, co
                "attn_bwd");
 }
 
+// Dispatcher-visible attention ops on token-major rows, used by the graph rewriter's filtered
+// attention node (centrifuge_b200._filter_C) for SDPA graphs of arbitrary models.
+std::tuple<Tensor, Tensor> attn_fwd_rows(const Tensor& qkv, int64_t B, int64_t S, int64_t nh,
+                                         int64_t nkv, int64_t hd, double scale) {
+  Tensor out = at::empty({B * S, nh * hd}, qkv.options());
+  Tensor lse = at::empty({B * S, nh}, qkv.options().dtype(at::kFloat));
+  attn_fwd(qkv, out, lse, B, S, nh, nkv, hd, scale);
+  return {out, lse};
+}
+
+Tensor attn_bwd_rows(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k,
+                     const Tensor& do_k, const Tensor& lse_k, const Tensor& pos_k, int64_t B,
+                     int64_t S, int64_t Sk, int64_t nh, int64_t nkv, int64_t hd, double scale) {
+  Tensor dqkv = at::empty_like(qkv_k);
+  Tensor delta = at::empty({B * Sk * nh}, qkv_k.options().dtype(at::kFloat));
+  Tensor o = o_k.contiguous(), d = do_k.contiguous();
+  attn_bwd(qkv_k, qkv_full, o, d, lse_k, pos_k, dqkv, delta, B, S, Sk, nh, nkv, hd, scale);
+  return dqkv;
+}
+
 }  // namespace
+
+TORCH_LIBRARY(cfb, m) {
+  m.def("attn_fwd_rows(Tensor qkv, int B, int S, int nh, int nkv, int hd, float scale) -> "
+        "(Tensor, Tensor)");
+  m.def("attn_bwd_rows(Tensor qkv_k, Tensor qkv_full, Tensor o_k, Tensor do_k, Tensor lse_k, "
+        "Tensor pos_k, int B, int S, int Sk, int nh, int nkv, int hd, float scale) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(cfb, CUDA, m) {
+  m.impl("attn_fwd_rows", &attn_fwd_rows);
+  m.impl("attn_bwd_rows", &attn_bwd_rows);
+}
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of centrifuge_b200";
