@@ -81,7 +81,8 @@ class LlamaCore(torch.nn.Module):
 
     def __init__(self, cfg: LlamaConfig, device="cuda", first: int = 0, last: Optional[int] = None,
                  has_embed: bool = True, has_head: bool = True, seed: int = 0,
-                 init: bool = True, keep_logits: bool = False):
+                 init: bool = True, keep_logits: bool = False, dtype=torch.bfloat16,
+                 pad_to: int = 1):
         super().__init__()
         assert not cfg.tie_word_embeddings, "tied embeddings are not supported"
         self.cfg = cfg
@@ -90,7 +91,8 @@ class LlamaCore(torch.nn.Module):
         self.layer_ids = range(self.first, self.last)
         self.has_embed, self.has_head = has_embed, has_head
         self.keep_logits = keep_logits
-        self.flat = FlatParams(param_specs(cfg, self.layer_ids, has_embed, has_head), device)
+        self.flat = FlatParams(param_specs(cfg, self.layer_ids, has_embed, has_head), device,
+                               dtype=dtype, pad_to=pad_to)
         self.device = self.flat.device
         self.nh, self.nkv, self.hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         self.scale = 1.0 / math.sqrt(self.hd)
@@ -108,16 +110,13 @@ class LlamaCore(torch.nn.Module):
     # ------------------------------------------------------------------ parameters
     def reset_parameters(self, seed: int = 0) -> None:
         """HF Llama init: N(0, initializer_range) for matrices, ones for norms."""
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        g = torch.Generator(device=self.device).manual_seed(seed)
         std = self.cfg.initializer_range
         for name, p in self.flat.params.items():
             if p.dim() == 1:
                 p.fill_(1.0)
             else:
-                # generate on CPU in chunks for determinism across devices
-                t = torch.empty(p.shape, dtype=torch.float32)
-                t.normal_(0.0, std, generator=g)
-                p.copy_(t.to(p.device))
+                p.normal_(0.0, std, generator=g)
 
     def named_flat_parameters(self):
         return self.flat.params.items()
@@ -139,8 +138,7 @@ class LlamaCore(torch.nn.Module):
             B, S = input_ids.shape
         else:
             B, S = batch_shape
-        inp = hidden if hidden is not None else self._anchor
-        out = _CfLlamaFn.apply(inp, input_ids, labels, self, B, S)
+        out = _CfLlamaFn.apply(self._anchor, hidden, input_ids, labels, self, B, S)
         if self.has_head:
             res = CausalLMOutput(token_loss=out)
             if self.keep_logits and getattr(self, "_last_logits", None) is not None:
@@ -290,8 +288,8 @@ class _CfLlamaFn(torch.autograd.Function):
     :meth:`cf_attach` with the keep mask."""
 
     @staticmethod
-    def forward(ctx, inp, input_ids, labels, model: LlamaCore, B: int, S: int):
-        out, sv = model._forward_impl(input_ids, None if model.has_embed else inp, labels, B, S)
+    def forward(ctx, anchor, hidden, input_ids, labels, model: LlamaCore, B: int, S: int):
+        out, sv = model._forward_impl(input_ids, hidden, labels, B, S)
         ctx.model = model
         ctx.saved = sv
         ctx.slot = FilterSlot()
@@ -305,7 +303,7 @@ class _CfLlamaFn(torch.autograd.Function):
         if sv is None:
             raise RuntimeError("native Llama backward ran twice (retain_graph is not supported)")
         dx = ctx.model._backward_impl(sv, grad_out, ctx.slot.state)
-        return (dx if ctx.hidden_in else None), None, None, None, None, None
+        return None, (dx if ctx.hidden_in else None), None, None, None, None, None
 
     @staticmethod
     def cf_attach(ctx, mask: torch.Tensor) -> None:

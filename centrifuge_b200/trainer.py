@@ -1,0 +1,67 @@
+"""Filtered training step on the native B200 models.
+
+Per micro-batch: forward (fused lm_head + per-token CE), utility-based token selection
+(``token_filter_loss``), ``backward_filter`` on the loss, the filtered backward (gradients
+reduced on the fly by the ZeRO optimizer), and after ``grad_accum`` micro-batches one fused
+AdamW step.  Mirrors ``Trainer.train_step`` of the reference (train.py:222-326) without its
+host synchronisations: the only device-to-host read is the optional loss readout.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence
+
+import torch
+
+from .data.synthetic import Batch
+from .filter import backward_filter
+from .loss import keep_count, token_filter_loss
+
+
+class Trainer:
+    def __init__(self, model, optimizer, drop_rate: float = 0.5, strategy: str = "fixed",
+                 grad_accum: int = 1, world_size: int = 1, timer=None):
+        self.model = model
+        self.opt = optimizer
+        self.drop_rate = drop_rate
+        self.strategy = strategy
+        self.grad_accum = grad_accum
+        self.world = world_size
+        self.timer = timer
+        self.device = model.device
+        if hasattr(optimizer, "attach"):
+            optimizer.attach(model)
+
+    def micro_step(self, batch: Batch) -> torch.Tensor:
+        ids = batch.input_ids
+        B, S = ids.shape
+        out = self.model(ids)
+        mask = (batch.attention_mask.clone() if batch.attention_mask is not None else
+                torch.ones(B, S, dtype=torch.long, device=ids.device))
+        if self.drop_rate > 0:
+            loss, mask = token_filter_loss(ids, None, mask, batch.ref_loss, self.strategy,
+                                           self.drop_rate, True, True,
+                                           per_token_loss=out.token_loss)
+            if self.strategy == "fixed" and batch.attention_mask is None:
+                mask._cf_keep = keep_count(S, self.drop_rate)
+            backward_filter(loss, mask)
+        else:
+            loss = token_filter_loss(ids, None, mask, None, None, None, True,
+                                     per_token_loss=out.token_loss)
+        if hasattr(self.opt, "begin_micro"):
+            self.opt.begin_micro()
+        loss.backward()
+        if hasattr(self.opt, "end_micro"):
+            self.opt.end_micro()
+        return loss.detach()
+
+    def train_step(self, batches: Sequence[Batch], to_device: bool = True) -> torch.Tensor:
+        """One optimizer step over ``grad_accum`` micro-batches; returns the mean loss (device)."""
+        assert len(batches) == self.grad_accum
+        total = torch.zeros((), device=self.device)
+        for b in batches:
+            if to_device:
+                b = b.to(self.device, non_blocking=True)
+            total += self.micro_step(b)
+        self.opt.step(grad_scale=1.0 / (self.grad_accum * self.world))
+        self.opt.zero_grad()
+        return total / self.grad_accum
