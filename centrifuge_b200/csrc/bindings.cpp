@@ -343,6 +343,32 @@ void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, co
                "attn_bwd");
 }
 
+// ---- NVLink peer-memory gradient reduction (pointers are raw device addresses from the
+// symmetric-memory handle; `err` is a device int32 word)
+void symm_signal(int64_t peer_flags_dev, int64_t W, int64_t off, int64_t epoch) {
+  CFB_CHECK_RC(cfb_symm_signal(reinterpret_cast<uint32_t* const*>(peer_flags_dev), W, off,
+                               static_cast<uint32_t>(epoch), cur_stream()),
+               "symm_signal");
+}
+
+void symm_wait(int64_t flags, int64_t base, int64_t stride, int64_t n, int64_t epoch,
+               Tensor& err) {
+  CFB_CHECK_RC(cfb_symm_wait(reinterpret_cast<const uint32_t*>(flags), base, stride, n,
+                             static_cast<uint32_t>(epoch), err.data_ptr<int>(), cur_stream()),
+               "symm_wait");
+}
+
+void symm_pull_reduce(int64_t mc_base, int64_t peer_base_dev, int64_t W, int64_t off, int64_t n,
+                      Tensor& dst, double scale, Tensor& err) {
+  TORCH_CHECK(dst.scalar_type() == at::kFloat && dst.is_contiguous() && dst.numel() == n,
+              "symm_pull_reduce: dst must be a contiguous fp32 [n] tensor");
+  CFB_CHECK_RC(cfb_symm_pull_reduce(reinterpret_cast<const float*>(mc_base),
+                                    reinterpret_cast<const float* const*>(peer_base_dev), W, off,
+                                    n, dst.data_ptr<float>(), static_cast<float>(scale), nullptr,
+                                    0, 0, err.data_ptr<int>(), cur_stream()),
+               "symm_pull_reduce");
+}
+
 // Dispatcher-visible attention ops on token-major rows, used by the graph rewriter's filtered
 // attention node (centrifuge_b200._filter_C) for SDPA graphs of arbitrary models.
 std::tuple<Tensor, Tensor> attn_fwd_rows(const Tensor& qkv, int64_t B, int64_t S, int64_t nh,
@@ -402,6 +428,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_f32", &scale_f32);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
+  m.def("symm_signal", &symm_signal);
+  m.def("symm_wait", &symm_wait);
+  m.def("symm_pull_reduce", &symm_pull_reduce);
   m.attr("EPI_BF16") = static_cast<int>(kEpiBF16);
   m.attr("EPI_BF16_RESID") = static_cast<int>(kEpiBF16Resid);
   m.attr("EPI_F32") = static_cast<int>(kEpiF32);

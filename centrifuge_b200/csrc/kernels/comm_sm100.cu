@@ -1,0 +1,141 @@
+// Gradient reduce-scatter over NVLink peer memory, fused with the fp32 accumulation into the
+// rank's ZeRO-2 gradient shard (sm_100a).
+//
+// Every rank's flat fp32 gradient buffer lives in symmetric memory (same offsets on every
+// GPU).  For a bucket [lo, hi), rank r owns chunk r.  Protocol per micro-batch `epoch`:
+//   1. bucket ready: after the backward has produced bucket b, each rank stores `epoch` into
+//      ready[b * W + me] of every peer's flag buffer (release, system scope);
+//   2. pull-reduce: each rank waits (bounded, in a one-block kernel so that no SMs spin) until
+//      ready[b * W + p] >= epoch for all p, then reads its chunk from every rank and adds the
+//      sum into its fp32 shard:
+//        * NVLS: one multimem.ld_reduce.add.v4.f32 per 16 bytes on the multicast address --
+//          the NVSwitch sums the W copies, each GPU receives one reduced copy;
+//        * otherwise plain 16-byte loads from each peer's buffer;
+//   3. micro-batch done: after its last bucket each rank stores `epoch` into done[me] of every
+//      peer and waits (bounded) for done[p] >= epoch of all peers before its gradient buffer is
+//      cleared for the next micro-batch.
+// Waits give up after a time limit and record an error code in a device word that the host
+// reads; they never trap.  No TMA and no cluster multicast are used here.
+#include "sm100_common.cuh"
+#include "launch_api.h"
+
+namespace cfb {
+namespace comm {
+
+constexpr uint64_t kFlagWaitNs = 20000000000ull;  // 20 s
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 multimem_ld_reduce_add_v4(const float* mc) {
+  float4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+
+// Wait until flags[base + i*stride] >= epoch for i < n.  Returns false on timeout.
+__device__ bool wait_flags(const uint32_t* flags, int base, int stride, int n, uint32_t epoch,
+                           int* err, int code) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int i = 0; i < n; ++i) {
+    const uint32_t* f = flags + base + i * stride;
+    uint32_t spins = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
+      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kFlagWaitNs) {
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// One thread per peer stores `epoch` at offset `off` of that peer's flag buffer.
+__global__ void signal_peers_kernel(uint32_t* const* peer_flags, int W, int off, uint32_t epoch) {
+  const int p = threadIdx.x;
+  if (p < W) {
+    __threadfence_system();
+    st_release_sys(peer_flags[p] + off, epoch);
+  }
+}
+
+__global__ void wait_kernel(const uint32_t* flags, int base, int stride, int n, uint32_t epoch,
+                            int* err) {
+  if (threadIdx.x == 0) wait_flags(flags, base, stride, n, epoch, err, kErrPeerWait);
+}
+
+// dst[i] += scale * sum_p src_p[off + i]  for i < n  (n % 4 == 0, 16-byte aligned)
+__global__ void __launch_bounds__(512) pull_reduce_kernel(
+    const float* mc_base, const float* const* peer_base, int W, long long off, long long n,
+    float* __restrict__ dst, float scale, const uint32_t* flags, int bucket, uint32_t epoch,
+    int* err) {
+  if (flags != nullptr) {  // optional in-kernel wait (the host path waits in wait_kernel)
+    __shared__ int ok;
+    if (threadIdx.x == 0)
+      ok = wait_flags(flags, bucket * W, 1, W, epoch, err, kErrPeerWait) ? 1 : 0;
+    __syncthreads();
+    if (!ok) return;
+  }
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 s;
+    if (mc_base != nullptr) {
+      s = multimem_ld_reduce_add_v4(mc_base + off + 4 * i);
+    } else {
+      s = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int p = 0; p < W; ++p) {
+        const float4 v = *reinterpret_cast<const float4*>(peer_base[p] + off + 4 * i);
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+      }
+    }
+    float4 d = reinterpret_cast<float4*>(dst)[i];
+    d.x += scale * s.x;
+    d.y += scale * s.y;
+    d.z += scale * s.z;
+    d.w += scale * s.w;
+    reinterpret_cast<float4*>(dst)[i] = d;
+  }
+}
+
+}  // namespace comm
+}  // namespace cfb
+
+using namespace cfb::comm;
+
+int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,
+                    cudaStream_t st) {
+  if (W <= 0 || W > 1024) return -11;
+  signal_peers_kernel<<<1, 32 * ((W + 31) / 32), 0, st>>>(peer_flags_dev, W, off, epoch);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int cfb_symm_wait(const uint32_t* flags, int base, int stride, int n, uint32_t epoch, int* err,
+                  cudaStream_t st) {
+  wait_kernel<<<1, 32, 0, st>>>(flags, base, stride, n, epoch, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int cfb_symm_pull_reduce(const float* mc_base, const float* const* peer_base_dev, int W,
+                         long long off, long long n, float* dst, float scale,
+                         const uint32_t* flags, int bucket, uint32_t epoch, int* err,
+                         cudaStream_t st) {
+  if ((n % 4) != 0 || (off % 4) != 0) return -11;
+  if (n == 0) return 0;
+  long long blocks = (n / 4 + 511) / 512;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  pull_reduce_kernel<<<static_cast<int>(blocks), 512, 0, st>>>(
+      mc_base, peer_base_dev, W, off, n, dst, scale, flags, bucket, epoch, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}

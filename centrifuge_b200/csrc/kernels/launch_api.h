@@ -56,3 +56,13 @@ int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, cons
                  long long ld_o, const void* do_k, const float* lse_k, const int* pos_k,
                  void* dqkv_k, float* unused, float* delta, int B, int S, int Sk, int nh,
                  int nkv, int hd, float scale, cudaStream_t st);
+
+// NVLink peer-memory gradient reduction (comm_sm100.cu).
+int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,
+                    cudaStream_t st);
+int cfb_symm_wait(const uint32_t* flags, int base, int stride, int n, uint32_t epoch, int* err,
+                  cudaStream_t st);
+int cfb_symm_pull_reduce(const float* mc_base, const float* const* peer_base_dev, int W,
+                         long long off, long long n, float* dst, float scale,
+                         const uint32_t* flags, int bucket, uint32_t epoch, int* err,
+                         cudaStream_t st);

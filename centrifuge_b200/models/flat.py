@@ -50,6 +50,18 @@ class FlatParams:
             self.params[name] = self.data[o:o + n].view(shape)
             self.grads[name] = self.grad[o:o + n].view(shape)
 
+    def rebind_grad(self, buf: torch.Tensor) -> None:
+        """Move the gradient storage to ``buf`` (e.g. symmetric memory for peer access)."""
+        assert buf.numel() == self.numel and buf.dtype == self.grad.dtype
+        buf.copy_(self.grad)
+        self.grad = buf
+        for name, shape in self.specs.items():
+            o = self.offsets[name]
+            n = 1
+            for d in shape:
+                n *= d
+            self.grads[name] = self.grad[o:o + n].view(shape)
+
     def names(self) -> List[str]:
         return list(self.specs)
 

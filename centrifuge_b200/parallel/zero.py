@@ -64,6 +64,13 @@ class NcclReducer:
         self._send = None
         self._recv = None
 
+    def reduce_bucket(self, idx: int, b, src_fp32: torch.Tensor, dst_fp32: torch.Tensor) -> None:
+        self.reduce_scatter_acc(src_fp32, dst_fp32, 1.0)
+        src_fp32.zero_()
+
+    def end_micro(self, flat) -> None:
+        pass
+
     def reduce_scatter_acc(self, src_fp32: torch.Tensor, dst_fp32: torch.Tensor, scale: float):
         n, c = src_fp32.numel(), dst_fp32.numel()
         if self._send is None or self._send.numel() < n:
@@ -109,6 +116,7 @@ class ZeroAdamW:
             chunk = (hi - lo) // self.W
             b = Bucket(lo, hi, chunk, off)
             b._own_lo = lo + self.rank * chunk
+            b.idx = len(self.buckets)
             self.buckets.append(b)
             off += chunk
             lo = hi
@@ -154,16 +162,14 @@ class ZeroAdamW:
     def _reduce_bucket(self, b: Bucket) -> None:
         src = self.flat.grad[b.lo:b.hi]
         dst = self.grad_shard[b.shard_off:b.shard_off + b.chunk]
+        idx = self.buckets.index(b) if not hasattr(b, "idx") else b.idx
         if self._comm_stream is not None:
             cur = torch.cuda.current_stream(self.device)
             self._comm_stream.wait_stream(cur)
             with torch.cuda.stream(self._comm_stream):
-                self.reducer.reduce_scatter_acc(src, dst, 1.0)
-                src.zero_()
-            src.record_stream(self._comm_stream)
+                self.reducer.reduce_bucket(idx, b, src, dst)
         else:
-            self.reducer.reduce_scatter_acc(src, dst, 1.0)
-            src.zero_()
+            self.reducer.reduce_bucket(idx, b, src, dst)
 
     def end_micro(self) -> None:
         """Finish the micro-batch: reduce what is left (stage 2) and join the comm stream."""
@@ -171,8 +177,16 @@ class ZeroAdamW:
             return
         if self.stage == 2:
             self.on_grads_ready(0, self.flat.numel)
+            self._finish_reducer()
         if self._comm_stream is not None:
             torch.cuda.current_stream(self.device).wait_stream(self._comm_stream)
+
+    def _finish_reducer(self) -> None:
+        if self._comm_stream is not None:
+            with torch.cuda.stream(self._comm_stream):
+                self.reducer.end_micro(self.flat)
+        else:
+            self.reducer.end_micro(self.flat)
 
     # ------------------------------------------------------------------ step
     def zero_grad(self) -> None:
@@ -186,6 +200,7 @@ class ZeroAdamW:
     def _reduce_all_stage1(self) -> None:
         for b in self.buckets:
             self._reduce_bucket(b)
+        self._finish_reducer()
         if self._comm_stream is not None:
             torch.cuda.current_stream(self.device).wait_stream(self._comm_stream)
 
