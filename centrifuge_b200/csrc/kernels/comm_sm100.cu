@@ -15,7 +15,7 @@
 //      peer and waits (bounded) for done[p] >= epoch of all peers before its gradient buffer is
 //      cleared for the next micro-batch.
 // Waits give up after a time limit and record an error code in a device word that the host
-// reads; they never trap.  No TMA and no cluster multicast are used here.
+// reads; they never trap.  No TMA is used here.
 #include "sm100_common.cuh"
 #include "launch_api.h"
 

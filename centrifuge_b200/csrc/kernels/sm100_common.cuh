@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a kernels: mbarriers with bounded waits, TMA tile
-// loads (no cluster multicast anywhere in this code base), tcgen05 MMA / TMEM access and the
+// loads into the issuing CTA's own shared memory, tcgen05 MMA / TMEM access and the
 // UMMA shared-memory / instruction descriptors.
 //
 // Descriptor bit layouts follow the public PTX ISA description of tcgen05 matrix and
