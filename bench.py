@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--mbs", type=int, default=8)
     ap.add_argument("--ga", type=int, default=4)
     ap.add_argument("--drop", type=float, default=0.5)
+    ap.add_argument("--mode", default="centrifuge", choices=["regular", "loss_only", "centrifuge"],
+                    help="regular: no filtering; loss_only: filtered loss, dense backward; "
+                         "centrifuge: filtered loss and filtered backward")
     ap.add_argument("--zero", type=int, default=2)
     ap.add_argument("--reducer", default="auto", choices=["auto", "nccl", "symm"])
     ap.add_argument("--no-e2e", action="store_true")
@@ -162,7 +165,9 @@ def main():
                 print(f"symmetric-memory reducer unavailable ({e}); using NCCL", file=sys.stderr)
     opt = ZeroAdamW(model.flat, group=group, stage=args.zero, lr=1e-4, betas=(0.9, 0.95),
                     eps=1e-8, weight_decay=0.0, grad_clip=1.0, reducer=reducer)
-    trainer = Trainer(model, opt, drop_rate=args.drop, grad_accum=args.ga, world_size=world)
+    drop = 0.0 if args.mode == "regular" else args.drop
+    trainer = Trainer(model, opt, drop_rate=drop, grad_accum=args.ga, world_size=world,
+                      filter_backward=args.mode == "centrifuge")
     data = SyntheticTokenData(cfg.vocab_size, args.mbs, args.seq, seed=4321, rank=rank)
 
     def barrier():
@@ -226,8 +231,10 @@ def main():
             "data": "synthetic (uniform token ids, LogNormal(1.0,0.5) ref_loss, random-init weights)",
             "config": {"model": cfg.name, "global_batch": world * args.ga * args.mbs,
                        "micro_batch": args.mbs, "grad_accum": args.ga, "seq_len": args.seq,
-                       "drop_rate": args.drop, "parallelism": f"zero{args.zero}-dp{world}",
-                       "reducer": type(opt.reducer).__name__ if opt.reducer else "none",
+                       "drop_rate": drop, "mode": args.mode,
+                       "parallelism": f"zero{args.zero}-dp{world}",
+                       "reducer": (getattr(opt.reducer, "kind", type(opt.reducer).__name__)
+                                   if opt.reducer else "none"),
                        "l2": "working set (weights + activations) far larger than L2"},
             "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
             "loss": float(loss.item()),

@@ -19,7 +19,8 @@ from .loss import keep_count, token_filter_loss
 
 class Trainer:
     def __init__(self, model, optimizer, drop_rate: float = 0.5, strategy: str = "fixed",
-                 grad_accum: int = 1, world_size: int = 1, timer=None):
+                 grad_accum: int = 1, world_size: int = 1, timer=None,
+                 filter_backward: bool = True):
         self.model = model
         self.opt = optimizer
         self.drop_rate = drop_rate
@@ -27,6 +28,8 @@ class Trainer:
         self.grad_accum = grad_accum
         self.world = world_size
         self.timer = timer
+        # False = "loss only": the selection masks the loss but the backward stays dense
+        self.filter_backward = filter_backward
         self.device = model.device
         if hasattr(optimizer, "attach"):
             optimizer.attach(model)
@@ -43,7 +46,8 @@ class Trainer:
                                            per_token_loss=out.token_loss)
             if self.strategy == "fixed" and batch.attention_mask is None:
                 mask._cf_keep = keep_count(S, self.drop_rate)
-            backward_filter(loss, mask)
+            if self.filter_backward:
+                backward_filter(loss, mask)
         else:
             loss = token_filter_loss(ids, None, mask, None, None, None, True,
                                      per_token_loss=out.token_loss)
