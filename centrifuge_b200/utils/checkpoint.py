@@ -148,12 +148,27 @@ def load_model_(model, path: str) -> None:
     hf_to_native_(model.cfg, load_pretrained_state(path), dict(model.flat.params))
 
 
+def _sha256(path: str) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for blk in iter(lambda: f.read(1 << 20), b""):
+            h.update(blk)
+    return h.hexdigest()
+
+
 def save_training_state(path: str, rank: int, shard_state: Dict[str, torch.Tensor],
                         client_state: Dict) -> None:
+    """Write this rank's optimizer shard (with a sha256 sidecar) and, on rank 0, the client
+    state ``{"step", "completed_steps"}``."""
     d = os.path.join(path, "training_states")
     os.makedirs(d, exist_ok=True)
-    torch.save({k: v.detach().cpu() for k, v in shard_state.items()},
-               os.path.join(d, f"optim_rank{rank}.pt"))
+    f = os.path.join(d, f"optim_rank{rank}.pt")
+    tmp = f + ".tmp"
+    torch.save({k: v.detach().cpu() for k, v in shard_state.items()}, tmp)
+    os.replace(tmp, f)
+    with open(f + ".sha256", "w") as fh:
+        fh.write(_sha256(f))
     if rank == 0:
         with open(os.path.join(d, "client_state.json"), "w") as f:
             json.dump(client_state, f)
@@ -162,8 +177,15 @@ def save_training_state(path: str, rank: int, shard_state: Dict[str, torch.Tenso
 
 
 def load_training_state(path: str, rank: int):
+    """Read this rank's shard (verifying its checksum) and the client state."""
     d = os.path.join(path, "training_states")
-    shard = torch.load(os.path.join(d, f"optim_rank{rank}.pt"), map_location="cpu")
+    f = os.path.join(d, f"optim_rank{rank}.pt")
+    if os.path.exists(f + ".sha256"):
+        with open(f + ".sha256") as fh:
+            want = fh.read().strip()
+        if _sha256(f) != want:
+            raise RuntimeError(f"training state {f}: checksum mismatch (corrupted shard)")
+    shard = torch.load(f, map_location="cpu")
     with open(os.path.join(d, "client_state.json")) as f:
         client = json.load(f)
     return shard, client

@@ -14,7 +14,7 @@ def free_port() -> int:
     return p
 
 
-def _entry(rank, world, port, fn, args, q):
+def _entry(rank, world, port, fn, args, q, pg_timeout=60):
     import datetime
 
     import torch.distributed as dist
@@ -22,7 +22,7 @@ def _entry(rank, world, port, fn, args, q):
                       WORLD_SIZE=str(world), LOCAL_RANK=str(rank))
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world,
-                                timeout=datetime.timedelta(seconds=60))
+                                timeout=datetime.timedelta(seconds=pg_timeout))
         out = fn(rank, world, *args)
         q.put((rank, "ok", out))
     except Exception:
@@ -32,17 +32,19 @@ def _entry(rank, world, port, fn, args, q):
             dist.destroy_process_group()
 
 
-def run_ranks(fn, world: int, *args, timeout: float = 240):
+def run_ranks(fn, world: int, *args, timeout: float = 240, pg_timeout: float = 60,
+              expect=None):
     """Run ``fn(rank, world, *args)`` on ``world`` gloo ranks; returns results by rank."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q)) for r in range(world)]
+    procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, q, pg_timeout))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
     try:
-        for _ in range(world):
+        for _ in range(expect if expect is not None else world):
             rank, status, out = q.get(timeout=timeout)
             if status != "ok":
                 raise AssertionError(f"rank {rank} failed:\n{out}")
@@ -52,4 +54,4 @@ def run_ranks(fn, world: int, *args, timeout: float = 240):
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
-    return [results[r] for r in range(world)]
+    return results if expect is not None else [results[r] for r in range(world)]
