@@ -215,7 +215,7 @@ void ce_fwd(const Tensor& logits, const Tensor& labels, Tensor& loss, Tensor& ls
 }
 
 void ce_bwd(const Tensor& logits, const c10::optional<Tensor>& rows, const Tensor& labels,
-            const Tensor& lse, const Tensor& dloss, Tensor& dlogits) {
+            const Tensor& lse, const Tensor& dloss, Tensor& dlogits, int64_t vocab_start) {
   check_bf16_2d(logits, "logits");
   check_bf16_2d(dlogits, "dlogits");
   TORCH_CHECK(dloss.scalar_type() == at::kFloat && dloss.numel() == dlogits.size(0), "dloss");
@@ -224,8 +224,22 @@ void ce_bwd(const Tensor& logits, const c10::optional<Tensor>& rows, const Tenso
   CFB_CHECK_RC(cfb_ce_bwd(logits.data_ptr(), logits.stride(0), opt_ptr<int>(rows),
                           reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()), lse.data_ptr<float>(),
                           dloss.data_ptr<float>(), dlogits.data_ptr(), dlogits.stride(0),
-                          dlogits.size(0), logits.size(1), cur_stream()),
+                          dlogits.size(0), logits.size(1), vocab_start, cur_stream()),
                "ce_bwd");
+}
+
+void ce_partial(const Tensor& logits, const Tensor& labels, Tensor& pmax, Tensor& psum,
+                Tensor& ptgt, int64_t vocab_start) {
+  check_bf16_2d(logits, "logits");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.numel() == logits.size(0), "labels");
+  if (logits.size(0) == 0) return;
+  const c10::cuda::CUDAGuard guard(logits.device());
+  CFB_CHECK_RC(cfb_ce_partial(logits.data_ptr(), logits.stride(0),
+                              reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                              pmax.data_ptr<float>(), psum.data_ptr<float>(),
+                              ptgt.data_ptr<float>(), logits.size(0), logits.size(1),
+                              vocab_start, cur_stream()),
+               "ce_partial");
 }
 
 void adamw(Tensor& master, const Tensor& grad, Tensor& m, Tensor& v, Tensor& param, double lr,
@@ -418,7 +432,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &embedding_fwd);
   m.def("embedding_bwd", &embedding_bwd);
   m.def("ce_fwd", &ce_fwd);
-  m.def("ce_bwd", &ce_bwd);
+  m.def("ce_bwd", &ce_bwd, py::arg("logits"), py::arg("rows"), py::arg("labels"),
+        py::arg("lse"), py::arg("dloss"), py::arg("dlogits"), py::arg("vocab_start") = 0);
+  m.def("ce_partial", &ce_partial);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);

@@ -350,12 +350,45 @@ __global__ void __launch_bounds__(256) ce_fwd_kernel(const __nv_bfloat16* __rest
   }
 }
 
-// dlogits[i, v] = (softmax(logits[src_i])[v] - [v == label]) * dloss[i]
+// dlogits[i, v] = (softmax(logits[src_i])[v] - [v == label]) * dloss[i]; with a vocabulary
+// shard the columns are global vocabulary ids vocab_start + v.
+
+// Vocabulary-parallel partial statistics of one shard: row max, sum of exp(logit - max) and
+// the logit of the label when it falls in [vocab_start, vocab_start + V) (else 0).
+__global__ void __launch_bounds__(256) ce_partial_kernel(
+    const __nv_bfloat16* __restrict__ logits, long long ld, const long long* __restrict__ labels,
+    float* __restrict__ pmax, float* __restrict__ psum, float* __restrict__ ptgt, int V,
+    long long vocab_start) {
+  __shared__ float sm_m[8], sm_s[8];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* lr = logits + static_cast<long long>(row) * ld;
+  float m = -CUDART_INF_F, s = 0.f;
+  for (int c = threadIdx.x * 8; c < V; c += 256 * 8) {
+    float f[8];
+    load8(lr + c, f);
+    float lm = f[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) lm = fmaxf(lm, f[i]);
+    const float nm = fmaxf(m, lm);
+    float acc = (m == -CUDART_INF_F) ? 0.f : s * __expf(m - nm);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += __expf(f[i] - nm);
+    s = acc;
+    m = nm;
+  }
+  block_max_sum(m, s, sm_m, sm_s);
+  if (threadIdx.x == 0) {
+    pmax[row] = m;
+    psum[row] = s;
+    const long long lab = labels[row] - vocab_start;
+    ptgt[row] = (labels[row] >= 0 && lab >= 0 && lab < V) ? __bfloat162float(lr[lab]) : 0.f;
+  }
+}
 __global__ void __launch_bounds__(256) ce_bwd_kernel(
     const __nv_bfloat16* __restrict__ logits, long long ld, const int* __restrict__ logit_rows,
     const long long* __restrict__ labels, const float* __restrict__ lse,
     const float* __restrict__ dloss, __nv_bfloat16* __restrict__ dlogits, long long ld_out,
-    int V) {
+    int V, long long vocab_start) {
   const int row = blockIdx.x;
   const long long src = logit_rows ? logit_rows[row] : row;
   const __nv_bfloat16* lr = logits + src * ld;
@@ -369,7 +402,7 @@ __global__ void __launch_bounds__(256) ce_bwd_kernel(
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float p = __expf(f[i] - l);
-      if (c + i == lab) p -= 1.f;
+      if (c + i + vocab_start == lab) p -= 1.f;
       f[i] = (lab >= 0) ? p * g : 0.f;
     }
     store8(out + c, f);
@@ -673,11 +706,22 @@ int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float*
 
 int cfb_ce_bwd(const void* logits, long long ld, const int* logit_rows, const long long* labels,
                const float* lse, const float* dloss, void* dlogits, long long ld_out, int rows,
-               int V, cudaStream_t st) {
+               int V, long long vocab_start, cudaStream_t st) {
   if (V % 8 || ld % 8 || ld_out % 8) return -11;
   if (rows == 0) return 0;
   ce_bwd_kernel<<<rows, 256, 0, st>>>(static_cast<const bf16*>(logits), ld, logit_rows, labels,
-                                      lse, dloss, static_cast<bf16*>(dlogits), ld_out, V);
+                                      lse, dloss, static_cast<bf16*>(dlogits), ld_out, V,
+                                      vocab_start);
+  return last_err();
+}
+
+int cfb_ce_partial(const void* logits, long long ld, const long long* labels, float* pmax,
+                   float* psum, float* ptgt, int rows, int V, long long vocab_start,
+                   cudaStream_t st) {
+  if (V % 8 || ld % 8) return -11;
+  if (rows == 0) return 0;
+  ce_partial_kernel<<<rows, 256, 0, st>>>(static_cast<const bf16*>(logits), ld, labels, pmax,
+                                          psum, ptgt, V, vocab_start);
   return last_err();
 }
 

@@ -34,7 +34,10 @@ int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float*
                float* lse, int rows, int V, cudaStream_t st);
 int cfb_ce_bwd(const void* logits, long long ld, const int* logit_rows, const long long* labels,
                const float* lse, const float* dloss, void* dlogits, long long ld_out, int rows,
-               int V, cudaStream_t st);
+               int V, long long vocab_start, cudaStream_t st);
+int cfb_ce_partial(const void* logits, long long ld, const long long* labels, float* pmax,
+                   float* psum, float* ptgt, int rows, int V, long long vocab_start,
+                   cudaStream_t st);
 int cfb_adamw(float* master, const float* grad, float* m, float* v, void* param_bf16, long long n,
               float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2,
               const float* grad_scale, cudaStream_t st);

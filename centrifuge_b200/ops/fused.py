@@ -137,16 +137,46 @@ def ce_fwd(logits: torch.Tensor, labels: torch.Tensor, loss: Optional[torch.Tens
 
 
 def ce_bwd(logits: torch.Tensor, labels: torch.Tensor, lse: torch.Tensor, dloss: torch.Tensor,
-           rows: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None):
+           rows: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+           vocab_start: int = 0):
+    """dlogits of the rows ``rows`` (all when None); with a vocabulary shard the logits'
+    columns are the global ids ``vocab_start + j`` and ``lse`` is the full-vocabulary lse."""
     n = dloss.numel()
     if out is None:
         out = torch.empty(n, logits.shape[1], dtype=logits.dtype, device=logits.device)
     if not logits.is_cuda:
         r = torch.arange(logits.shape[0]) if rows is None else rows.long()
-        out.copy_(ref.cross_entropy_bwd(logits[r], labels[r], lse[r], dloss))
+        lab = labels[r]
+        V = logits.shape[1]
+        p = torch.exp(logits[r].float() - lse[r].unsqueeze(-1))
+        loc = lab - vocab_start
+        hit = (lab >= 0) & (loc >= 0) & (loc < V)
+        p[hit, loc[hit]] -= 1.0
+        p = p * dloss.unsqueeze(-1)
+        p[lab < 0] = 0
+        out.copy_(p)
         return out
-    kernels().ce_bwd(logits, rows, labels, lse, dloss, out)
+    kernels().ce_bwd(logits, rows, labels, lse, dloss, out, vocab_start)
     return out
+
+
+def ce_partial(logits: torch.Tensor, labels: torch.Tensor, vocab_start: int):
+    """Per-row (max, sum exp(logit - max), label logit or 0) of one vocabulary shard."""
+    rows = logits.shape[0]
+    f32 = dict(dtype=torch.float32, device=logits.device)
+    pmax, psum, ptgt = (torch.empty(rows, **f32) for _ in range(3))
+    if not logits.is_cuda:
+        lf = logits.float()
+        pmax.copy_(lf.max(-1).values)
+        psum.copy_(torch.exp(lf - pmax.unsqueeze(-1)).sum(-1))
+        loc = labels - vocab_start
+        hit = (labels >= 0) & (loc >= 0) & (loc < lf.shape[1])
+        t = torch.zeros(rows, **f32)
+        t[hit] = lf[hit, loc[hit]]
+        ptgt.copy_(t)
+        return pmax, psum, ptgt
+    kernels().ce_partial(logits, labels, pmax, psum, ptgt, vocab_start)
+    return pmax, psum, ptgt
 
 
 # ---------------------------------------------------------------- optimizer

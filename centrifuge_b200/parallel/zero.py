@@ -93,7 +93,7 @@ class ZeroAdamW:
     def __init__(self, flat: FlatParams, group=None, stage: int = 2, lr: float = 1e-4,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0,
                  grad_clip: float = 1.0, bucket_numel: int = 1 << 26, reducer=None,
-                 overlap: bool = True):
+                 overlap: bool = True, norm_group=None, replicated_ranges=()):
         assert stage in (1, 2)
         self.flat = flat
         self.group = group
@@ -143,6 +143,16 @@ class ZeroAdamW:
         self._comm_stream = torch.cuda.Stream(device=self.device) if self.overlap else None
         self._ready = 0  # buckets reduced in the current micro-batch
         self.grad_scale = 1.0
+        # Model-parallel group whose ranks hold different shards of the model: the grad-norm
+        # sums over it; ``replicated_ranges`` (flat [lo, hi) ranges of parameters replicated on
+        # every rank of that group) are counted once.
+        self.norm_group = norm_group
+        self.norm_world = dist.get_world_size(norm_group) if norm_group is not None else 1
+        self.replicated_ranges = list(replicated_ranges)
+        if self.replicated_ranges and self.norm_world > 1:
+            assert self.W == 1, "replicated-parameter norm correction needs data-parallel size 1"
+        # callables run at the start of step(), e.g. summing replicated gradients over TP
+        self.pre_step_hooks = []
 
     # ------------------------------------------------------------------ backward hooks
     def attach(self, model) -> None:
@@ -209,9 +219,22 @@ class ZeroAdamW:
         ``1 / (grad_accum * world)``).  Returns the (device) global grad-norm tensor."""
         if self.W > 1 and self.stage == 1:
             self._reduce_all_stage1()
+        for hook in self.pre_step_hooks:
+            hook()
         self.step_count += 1
         g = self.grad_shard
-        if self.W > 1:
+        if self.norm_world > 1:
+            tot = g.float().pow(2).sum().view(1)
+            if self.replicated_ranges:
+                rep = sum(g[lo:hi].float().pow(2).sum() for lo, hi in self.replicated_ranges)
+                tot = tot - (1.0 - 1.0 / self.norm_world) * rep
+            self._sumsq_total.copy_(tot)
+            if self.W > 1:
+                dist.all_reduce(self._sumsq_total, group=self.group)
+            dist.all_reduce(self._sumsq_total, group=self.norm_group)
+            fused.grad_norm_clip_coef(g, self.grad_clip, grad_scale, self._coef, self._norm,
+                                      extra_sumsq=self._sumsq_total)
+        elif self.W > 1:
             if g.is_cuda:
                 fused.kernels().sumsq(g, self._sumsq)
                 torch.sum(self._sumsq, dim=0, keepdim=True, out=self._sumsq_total)
