@@ -105,6 +105,8 @@ class TPLlamaCore(torch.nn.Module):
         self.grad_ready_hook = None
         self._anchor = torch.zeros((), device=self.device, requires_grad=True)
         self.replicated = replicated_names(self.flat.names())
+        self.pending_input_grad = None
+        self.last_state = None
 
     def reduce_replicated_grads(self) -> None:
         """Sum the gradients of replicated weights (embedding, RMSNorm) over the TP group.
@@ -293,7 +295,12 @@ class _CfTPLlamaFn(torch.autograd.Function):
     def backward(ctx, grad_out):
         sv, ctx.saved = ctx.saved, None
         dx = ctx.model._backward_impl(sv, grad_out, ctx.slot.state)
-        return None, (dx if ctx.hidden_in else None), None, None, None, None, None
+        if ctx.hidden_in:
+            # the input gradient is in the kept-row layout of the pipeline, not the input's
+            # shape: hand it to the pipeline schedule instead of autograd
+            ctx.model.pending_input_grad = dx
+        ctx.model.last_state = ctx.slot.state
+        return None, None, None, None, None, None, None
 
     @staticmethod
     def cf_attach(ctx, mask):

@@ -49,7 +49,8 @@ class Bucket:
 
 
 def _world(group):
-    if group is None and not (dist.is_available() and dist.is_initialized()):
+    """(size, rank) of the data-parallel group; ``None`` means no data parallelism."""
+    if group is None:
         return 1, 0
     return dist.get_world_size(group), dist.get_rank(group)
 
@@ -93,7 +94,8 @@ class ZeroAdamW:
     def __init__(self, flat: FlatParams, group=None, stage: int = 2, lr: float = 1e-4,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0,
                  grad_clip: float = 1.0, bucket_numel: int = 1 << 26, reducer=None,
-                 overlap: bool = True, norm_group=None, replicated_ranges=()):
+                 overlap: bool = True, norm_group=None, replicated_ranges=(),
+                 replication: Optional[int] = None):
         assert stage in (1, 2)
         self.flat = flat
         self.group = group
@@ -149,6 +151,7 @@ class ZeroAdamW:
         self.norm_group = norm_group
         self.norm_world = dist.get_world_size(norm_group) if norm_group is not None else 1
         self.replicated_ranges = list(replicated_ranges)
+        self.replication = replication or self.norm_world
         if self.replicated_ranges and self.norm_world > 1:
             assert self.W == 1, "replicated-parameter norm correction needs data-parallel size 1"
         # callables run at the start of step(), e.g. summing replicated gradients over TP
@@ -227,7 +230,7 @@ class ZeroAdamW:
             tot = g.float().pow(2).sum().view(1)
             if self.replicated_ranges:
                 rep = sum(g[lo:hi].float().pow(2).sum() for lo, hi in self.replicated_ranges)
-                tot = tot - (1.0 - 1.0 / self.norm_world) * rep
+                tot = tot - (1.0 - 1.0 / self.replication) * rep
             self._sumsq_total.copy_(tot)
             if self.W > 1:
                 dist.all_reduce(self._sumsq_total, group=self.group)
