@@ -1,0 +1,73 @@
+"""TP=2 (+SP) on 2 GPUs against the single-GPU native model (bf16 tolerance)."""
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from centrifuge_b200.config import tiny_llama_test
+        from centrifuge_b200.filter import backward_filter
+        from centrifuge_b200.loss import token_filter_loss
+        from centrifuge_b200.models.llama import NativeLlamaForCausalLM
+        from centrifuge_b200.models.tp_llama import TPLlamaCore, shard_full_params
+        os.environ["CFB_NODE_TRACING_FILE"] = f"/tmp/cfb_tp_dims_{rank}.txt"
+        cfg = tiny_llama_test(layers=2, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=1024,
+                              head_dim=64)
+        cfg.max_position_embeddings = 512
+        full = NativeLlamaForCausalLM(cfg, device="cuda", seed=0)
+        tp = TPLlamaCore(cfg, dist.group.WORLD, device="cuda")
+        tp.load_full_(dict(full.flat.params))
+        g = torch.Generator().manual_seed(3)
+        B, S = 2, 256
+        ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g).cuda()
+        rl = torch.exp(1.0 + 0.5 * torch.randn(B, S - 1, generator=g)).cuda()
+        res = {}
+        for name, m in (("full", full), ("tp", tp)):
+            out = m(ids)
+            loss, mask = token_filter_loss(ids, None, torch.ones(B, S, dtype=torch.long, device="cuda"),
+                                           rl, "fixed", 0.5, True, True, per_token_loss=out.token_loss)
+            backward_filter(loss, mask)
+            loss.backward()
+            if name == "tp":
+                m.reduce_replicated_grads()
+            res[name] = (float(loss.detach()), mask.cpu())
+        want = shard_full_params(cfg, {k: v.float() for k, v in full.flat.grads.items()}, world, rank)
+        errs = {k: float((tp.flat.grads[k].float() - want[k]).norm() / (want[k].norm() + 1e-12))
+                for k in want}
+        q.put((rank, res["full"][0], res["tp"][0], bool(torch.equal(res["full"][1], res["tp"][1])),
+               max(errs.values())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_gpu_matches_single_gpu():
+    import torch.multiprocessing as mp
+
+    from tests.dist_utils import free_port
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, lf, lt, same_mask, err in out:
+        assert abs(lf - lt) < 2e-2 * abs(lf)
+        if same_mask:
+            assert err < 5e-2, (rank, err)
