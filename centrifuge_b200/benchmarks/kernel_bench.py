@@ -52,8 +52,20 @@ def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3
     o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
     ms_f = _time(lambda: fused.attn_fwd(qkv, B, S, nh, nkv, hd, out=o, lse=lse), iters=10)
     fl_f = 4.0 * B * nh * hd * S * S / 2
-    res = [{"name": "attn_fwd", "ms": ms_f, "tflops": fl_f / ms_f / 1e9}]
+    res = [{"name": "attn_fwd_tcgen05", "ms": ms_f, "tflops": fl_f / ms_f / 1e9}]
     print(json.dumps(res[-1]))
+    from centrifuge_b200.ops import kernels
+    ms_m = _time(lambda: kernels().attn_fwd_mma(qkv, o, lse, B, S, nh, nkv, hd, 1.0 / hd ** 0.5),
+                 iters=10)
+    res.append({"name": "attn_fwd_mma_sync", "ms": ms_m, "tflops": fl_f / ms_m / 1e9})
+    print(json.dumps(res[-1]))
+    if hd == 128:
+        q64 = torch.randn(B * S, (nh + 2 * nkv) * 64, device="cuda").bfloat16()
+        o64, l64 = fused.attn_fwd(q64, B, S, nh, nkv, 64)
+        ms64 = _time(lambda: fused.attn_fwd(q64, B, S, nh, nkv, 64, out=o64, lse=l64), iters=10)
+        res.append({"name": "attn_fwd_tcgen05_hd64", "ms": ms64,
+                    "tflops": fl_f / 2 / ms64 / 1e9})
+        print(json.dumps(res[-1]))
     g = torch.Generator(device="cuda").manual_seed(0)
     for keep in keeps:
         Sk = int(S * keep) // 8 * 8

@@ -320,8 +320,8 @@ void scale_f32(Tensor& x, double s) {
   CFB_CHECK_RC(cfb_scale_f32(x.data_ptr<float>(), x.numel(), s, cur_stream()), "scale");
 }
 
-void attn_fwd(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S, int64_t nh,
-              int64_t nkv, int64_t hd, double scale) {
+void attn_fwd_mma(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S, int64_t nh,
+                  int64_t nkv, int64_t hd, double scale) {
   check_bf16_2d(qkv, "qkv");
   check_bf16_2d(out, "out");
   TORCH_CHECK(qkv.size(0) == B * S && out.size(0) == B * S, "attn_fwd: rows");
@@ -330,6 +330,21 @@ void attn_fwd(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S,
   const c10::cuda::CUDAGuard guard(qkv.device());
   CFB_CHECK_RC(cfb_attn_fwd(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0),
                             lse.data_ptr<float>(), B, S, nh, nkv, hd, scale, cur_stream()),
+               "attn_fwd");
+}
+
+// Causal GQA attention forward on tcgen05/TMEM (the production path).
+void attn_fwd(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S, int64_t nh,
+              int64_t nkv, int64_t hd, double scale) {
+  check_bf16_2d(qkv, "qkv");
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(qkv.size(0) == B * S && out.size(0) == B * S, "attn_fwd: rows");
+  TORCH_CHECK(qkv.size(1) >= (nh + 2 * nkv) * hd && out.size(1) >= nh * hd, "attn_fwd: cols");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == B * S * nh, "lse [T, nh] fp32");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  CFB_CHECK_RC(cfb_attn_fwd_tc(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0),
+                               lse.data_ptr<float>(), B, S, nh, nkv, hd, scale,
+                               err_word(qkv.get_device()).data_ptr<int>(), cur_stream()),
                "attn_fwd");
 }
 
@@ -443,6 +458,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cast_f32_bf16", &cast_f32_bf16);
   m.def("scale_f32", &scale_f32);
   m.def("attn_fwd", &attn_fwd);
+  m.def("attn_fwd_mma", &attn_fwd_mma);
   m.def("attn_bwd", &attn_bwd);
   m.def("symm_signal", &symm_signal);
   m.def("symm_wait", &symm_wait);

@@ -177,7 +177,8 @@ def test_drop_smallest_and_keep_index(S, drop):
 
 
 @pytest.mark.parametrize("B,S,nh,nkv,hd", [(2, 256, 4, 2, 64), (1, 200, 4, 1, 128),
-                                           (2, 512, 8, 2, 128)])
+                                           (2, 512, 8, 2, 128), (1, 1000, 4, 2, 64),
+                                           (1, 2048, 2, 1, 128), (3, 130, 2, 2, 64)])
 def test_attention_fwd(B, S, nh, nkv, hd):
     torch.manual_seed(9)
     ld = (nh + 2 * nkv) * hd
@@ -189,6 +190,12 @@ def test_attention_fwd(B, S, nh, nkv, hd):
     orf, lr = ref.attention(q, k, v)
     assert rel_err(o, orf.reshape(B * S, nh * hd)) < 1e-2
     assert rel_err(lse, lr.reshape(B * S, nh)) < 1e-4
+    from centrifuge_b200.ops import kernels
+    assert kernels().gemm_error_word(0, True) == 0
+    # the warp-level mma.sync forward agrees too
+    o2, l2 = torch.empty_like(o), torch.empty_like(lse)
+    kernels().attn_fwd_mma(qkv, o2, l2, B, S, nh, nkv, hd, 1.0 / hd ** 0.5)
+    assert rel_err(o2, o) < 1e-2 and rel_err(l2, lse) < 1e-4
 
 
 @pytest.mark.parametrize("B,S,nh,nkv,hd,keep", [(2, 256, 4, 2, 64, 0.5), (1, 320, 4, 1, 128, 0.3),
