@@ -4,8 +4,10 @@
 //   warp 0      TMA producer: Q once, then K_j / V_j tiles (2-stage ring) from the fused qkv rows
 //   warp 1      MMA issuer:   S_j = Q K_j^T into one of two TMEM tiles (128 x 128 fp32), then
 //                             O += P_j V_j into the TMEM accumulator (128 x hd fp32)
-//   warps 2-5   softmax:      one thread per query row (= TMEM lane): tcgen05.ld of its S row,
-//                             online softmax in fp32, P row written to shared memory as bf16
+//   warps 2-9   softmax:      two threads per query row (= TMEM lane): warps w and w+4 share a
+//                             lane quadrant and split the row's 128 keys (and O's hd columns)
+//                             in halves, exchanging the row max through shared memory;
+//                             online softmax in fp32, P written to shared memory as bf16
 //                             (128B-swizzled K-major operand of the PV MMA); the running max is
 //                             only moved (and O rescaled in TMEM) when it grows by more than
 //                             2^8, so most steps skip the rescale; epilogue O / l and LSE
@@ -38,7 +40,9 @@ struct Smem {
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KV_STAGES * KV_TILE;
   static constexpr int OFF_P = OFF_V + KV_STAGES * KV_TILE;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int OFF_RED = OFF_P + P_BYTES;  // [2 parity][2 half][128] max + [2 half][128] sum
+  static constexpr int OFF_FLAG = OFF_RED + 3 * 2 * BM * 4;  // [2 half][128] exchange counters
+  static constexpr int OFF_BAR = OFF_FLAG + 2 * BM * 4;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;     // + barriers + alignment slack
 };
 
@@ -60,8 +64,36 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
+// Exchange one float per row with the partner warp of the same lane quadrant.  Each side
+// publishes its value and a sequence number in shared memory and spins (bounded) until the
+// partner's sequence number arrives; values are double-buffered by sequence parity so a slot is
+// only rewritten after the partner has read it.  Returns false if the wait gave up.
+__device__ __forceinline__ bool pair_exchange(float* vals, volatile int* flags, int slot_base,
+                                              int half, int r, int seq, float mine, float& theirs,
+                                              volatile int* abort_flag, int* err) {
+  constexpr int BMr = 128;
+  vals[(slot_base + half) * BMr + r] = mine;
+  __threadfence_block();
+  flags[half * BMr + r] = seq;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (flags[(half ^ 1) * BMr + r] < seq) {
+    if ((++spins & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, kErrWaitSoftmax);
+        return false;
+      }
+    }
+  }
+  __threadfence_block();
+  theirs = vals[(slot_base + (half ^ 1)) * BMr + r];
+  return true;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, Params p) {
   using L = Smem<HD>;
   extern __shared__ uint8_t smem_raw[];
@@ -97,14 +129,16 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&s_full[s]), 1);
-      mbar_init(smem_u32(&s_free[s]), 4);
+      mbar_init(smem_u32(&s_free[s]), 8);
     }
-    mbar_init(smem_u32(p_ready), 4);
+    mbar_init(smem_u32(p_ready), 8);
     mbar_init(smem_u32(o_done), 1);
     mbar_init(smem_u32(drain), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
+  for (int i = threadIdx.x; i < 2 * BM; i += blockDim.x)
+    reinterpret_cast<volatile int*>(smem + L::OFF_FLAG)[i] = 0;
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
@@ -187,13 +221,19 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(smem_u32(drain), 0, &dummy, nullptr, 0);
     }
   } else {
-    // ------------------------------------------------------------------ softmax (warps 2..5)
+    // ------------------------------------------------------------------ softmax (warps 2..9)
+    constexpr int HALF = BN / 2;       // keys per thread
+    constexpr int OH = HD / 2;         // O columns per thread
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // query row in the tile == TMEM lane
+    const int half = (warp - 2) >> 2;  // 0: warps 2-5, 1: warps 6-9
+    const int r = quad * 32 + lane;    // query row in the tile == TMEM lane
     const int qpos = q0 + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+    volatile int* xflag = reinterpret_cast<volatile int*>(smem + L::OFF_FLAG);
+    int seq = 0;
     float m_ref = -CUDART_INF_F;  // log2-scaled running reference max
-    float l = 0.f;
+    float l = 0.f;                // partial row sum over this thread's keys
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       const int sb = j & 1;
@@ -202,24 +242,33 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sr[BN];
+      uint32_t sr[HALF];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) CFB_TMEM_LD32(lane_addr + sb * BN + c * 32, (sr + c * 32));
+      for (int c = 0; c < HALF / 32; ++c)
+        CFB_TMEM_LD32(lane_addr + sb * BN + half * HALF + c * 32, (sr + c * 32));
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
-      // scale, causal mask, row max
-      const int k0 = j * BN;
-      const bool diag = (k0 + BN - 1 > q0) || (k0 + BN > p.S);
+      // scale, causal mask, partial row max
+      const int k0 = j * BN + half * HALF;
+      const bool diag = (k0 + HALF - 1 > q0) || (k0 + HALF > p.S);
       float mx = -CUDART_INF_F;
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
+      for (int i = 0; i < HALF; ++i) {
         float v = __uint_as_float(sr[i]) * p.scale_log2;
         if (diag && (k0 + i > qpos || k0 + i >= p.S)) v = -CUDART_INF_F;
         sr[i] = __float_as_uint(v);
         mx = fmaxf(mx, v);
       }
+      // exchange the partial max with the partner warp
+      float other;
+      ++seq;
+      if (!pair_exchange(red, xflag, 2 * (seq & 1), half, r, seq, mx, other, abort_flag, p.err)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, other);
       const bool grow = (mx > m_ref + kRescaleThreshold) || (m_ref == -CUDART_INF_F);
       float alpha = 1.f;
       if (grow) {
@@ -229,9 +278,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       const float ref = (m_ref == -CUDART_INF_F) ? 0.f : m_ref;
       float rs = 0.f;
-      uint32_t pk[BN / 2];
+      uint32_t pk[HALF / 2];
 #pragma unroll
-      for (int i = 0; i < BN / 2; ++i) {
+      for (int i = 0; i < HALF / 2; ++i) {
         const float e0 = exp2f(__uint_as_float(sr[2 * i]) - ref);
         const float e1 = exp2f(__uint_as_float(sr[2 * i + 1]) - ref);
         rs += e0 + e1;
@@ -247,40 +296,39 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
+        for (int c = 0; c < OH / 32; ++c) {
           uint32_t o[32];
-          CFB_TMEM_LD32(lane_addr + o_col + c * 32, o);
+          CFB_TMEM_LD32(lane_addr + o_col + half * OH + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          CFB_TMEM_ST32(lane_addr + o_col + c * 32, o);
+          CFB_TMEM_ST32(lane_addr + o_col + half * OH + c * 32, o);
         }
         tmem_st_wait();
       }
-      // P row -> shared memory, K-major 128B-swizzled (2 chunks of 64 keys)
+      // this thread's 64 keys of the P row = K-chunk `half` of the PV operand (128B swizzle)
+      const uint32_t rowbase = sbase + L::OFF_P + half * L::CHUNK + r * 128;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const uint32_t rowbase = sbase + L::OFF_P + c * L::CHUNK + r * 128;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int w0 = c * 32 + i * 4;
-          st_shared_v4(rowbase + ((i ^ (r & 7)) << 4), pk[w0], pk[w0 + 1], pk[w0 + 2], pk[w0 + 3]);
-        }
-      }
+      for (int i = 0; i < 8; ++i)
+        st_shared_v4(rowbase + ((i ^ (r & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2],
+                     pk[4 * i + 3]);
       fence_async_shared();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(p_ready));
     }
-    // epilogue: O / l, LSE
+    // epilogue: combine the two partial row sums, O / l, LSE
     if (ok && mbar_wait(smem_u32(o_done), (nkb - 1) & 1, abort_flag, p.err, kErrWaitSoftmax)) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* dst = p.out + static_cast<long long>(row0 + qpos) * p.ld_out + h * HD;
+      float l_other = 0.f;
+      ok = pair_exchange(red, xflag, 4, half, r, ++seq, l, l_other, abort_flag, p.err);
+      const float lt = l + l_other;
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      __nv_bfloat16* dst = p.out + static_cast<long long>(row0 + qpos) * p.ld_out + h * HD + half * OH;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < OH / 32; ++c) {
         uint32_t o[32];
-        CFB_TMEM_LD32(lane_addr + o_col + c * 32, o);
+        CFB_TMEM_LD32(lane_addr + o_col + half * OH + c * 32, o);
         tmem_ld_wait();
         if (qpos < p.S) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
@@ -295,8 +343,8 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      if (qpos < p.S)
-        p.lse[static_cast<long long>(row0 + qpos) * p.nh + h] = (m_ref + log2f(l)) * kLn2;
+      if (qpos < p.S && half == 0)
+        p.lse[static_cast<long long>(row0 + qpos) * p.nh + h] = (m_ref + log2f(lt)) * kLn2;
     }
   }
 
@@ -332,7 +380,7 @@ int launch(const void* qkv, long long ld, void* out, long long ld_out, float* ls
     configured = true;
   }
   dim3 grid((S + BM - 1) / BM, nh, B);
-  kern<<<grid, 192, Smem<HD>::BYTES, st>>>(tm, p);
+  kern<<<grid, 320, Smem<HD>::BYTES, st>>>(tm, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
