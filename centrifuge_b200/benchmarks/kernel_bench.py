@@ -90,6 +90,9 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", default=None)
     ap.add_argument("--skip-attn", action="store_true")
+    ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--attn-shape", default="4,4096,32,8,128",
+                    help="B,S,nh,nkv,hd of the attention benchmark")
     args = ap.parse_args()
     shapes = [
         (8192, 8192, 8192, False, False, "square"),
@@ -100,9 +103,12 @@ def main():
         (2048, 5632, 8192, True, True, "tinyllama_down_wgrad_kept"),
         (16384, 32000, 2048, False, False, "tinyllama_lmhead_fwd"),
     ]
-    out = {"gemm": bench_gemm(shapes)}
+    out = {}
+    if not args.skip_gemm:
+        out["gemm"] = bench_gemm(shapes)
     if not args.skip_attn:
-        out["attention"] = bench_attention()
+        B, S, nh, nkv, hd = (int(x) for x in args.attn_shape.split(","))
+        out["attention"] = bench_attention(B, S, nh, nkv, hd)
     if args.json:
         with open(args.json, "w") as f:
             json.dump(out, f, indent=1)
