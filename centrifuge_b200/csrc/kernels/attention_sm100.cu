@@ -5,12 +5,14 @@
 //   warp 1      MMA issuer:   S_j = Q K_j^T into one of two TMEM tiles (128 x 128 fp32), then
 //                             O += P_j V_j into the TMEM accumulator (128 x hd fp32)
 //   warps 2-9   softmax:      two threads per query row (= TMEM lane): warps w and w+4 share a
-//                             lane quadrant and split the row's 128 keys (and O's hd columns)
-//                             in halves, exchanging the row max through shared memory;
-//                             online softmax in fp32, P written to shared memory as bf16
-//                             (128B-swizzled K-major operand of the PV MMA); the running max is
-//                             only moved (and O rescaled in TMEM) when it grows by more than
-//                             2^8, so most steps skip the rescale; epilogue O / l and LSE
+//                             lane quadrant and take keys [0, 64) / [64, 128) of every step.
+//                             Each half keeps its own running max, row sum and O accumulator
+//                             (O0, O1 in TMEM, fed by two K=64 PV MMAs), so the halves never
+//                             synchronise per step; the epilogue merges them once
+//                             (O = O0 2^(m0-m) + O1 2^(m1-m), same for l).  Online softmax in
+//                             fp32 with one FMA + ex2 per score, P written to shared memory as
+//                             bf16 (128B-swizzled K-major operand); a running max only moves
+//                             (and its O is rescaled in TMEM) when it grows by more than 2^8
 // S_{j+1} is issued before P_j V_j so that the tensor cores compute the next scores while the
 // softmax warps work on the current ones.  Q, K and V are read straight from the fused
 // [T, (nh + 2 nkv) hd] qkv rows with one 2-D tensor map (box 64 x 128): K tiles serve as the
@@ -40,7 +42,7 @@ struct Smem {
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + KV_STAGES * KV_TILE;
   static constexpr int OFF_P = OFF_V + KV_STAGES * KV_TILE;
-  static constexpr int OFF_RED = OFF_P + P_BYTES;  // [2 parity][2 half][128] max + [2 half][128] sum
+  static constexpr int OFF_RED = OFF_P + P_BYTES;  // epilogue exchange: [2][2 half][128] fp32
   static constexpr int OFF_FLAG = OFF_RED + 3 * 2 * BM * 4;  // [2 half][128] exchange counters
   static constexpr int OFF_BAR = OFF_FLAG + 2 * BM * 4;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;     // + barriers + alignment slack
@@ -56,6 +58,19 @@ struct Params {
   float scale_log2;
   int* err;
 };
+
+// Hardware base-2 exponential (MUFU); flushes denormal results to zero.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Three-input maximum (sm_100).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float y;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+  return y;
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -149,7 +164,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t o_col = 2 * BN;  // O accumulator after the two S tiles
+  const uint32_t o_col = 2 * BN;  // O0, O1 accumulators (HD columns each) after the S tiles
 
   if (warp == 0) {
     if (lane == 0) {
@@ -208,10 +223,12 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t vst = sbase + L::OFF_V + st * L::KV_TILE;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t aoff = (kk >> 2) * L::CHUNK + (kk & 3) * 32;
-          umma_bf16_ss(tmem + o_col, sdesc_sw128(sbase + L::OFF_P + aoff, 16, 1024),
+          // keys [0, 64) accumulate into O0, keys [64, 128) into O1
+          const int hh = kk >> 2;
+          const uint32_t aoff = hh * L::CHUNK + (kk & 3) * 32;
+          umma_bf16_ss(tmem + o_col + hh * HD, sdesc_sw128(sbase + L::OFF_P + aoff, 16, 1024),
                        sdesc_sw128(vst + kk * 2048, L::CHUNK, 1024), IDESC_O,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+                       (j > 0 || (kk & 3) > 0) ? 1u : 0u);
         }
         umma_commit(smem_u32(o_done));
         umma_commit(smem_u32(&kv_empty[st]));
@@ -222,18 +239,17 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax (warps 2..9)
-    constexpr int HALF = BN / 2;       // keys per thread
-    constexpr int OH = HD / 2;         // O columns per thread
+    constexpr int HALF = BN / 2;       // keys per thread per step
+    constexpr int OH = HD / 2;         // output columns per thread in the epilogue
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;  // 0: warps 2-5, 1: warps 6-9
     const int r = quad * 32 + lane;    // query row in the tile == TMEM lane
     const int qpos = q0 + r;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
-    volatile int* xflag = reinterpret_cast<volatile int*>(smem + L::OFF_FLAG);
-    int seq = 0;
-    float m_ref = -CUDART_INF_F;  // log2-scaled running reference max
-    float l = 0.f;                // partial row sum over this thread's keys
+    const uint32_t my_o = o_col + half * HD;
+    const float c = p.scale_log2;
+    float m_ref = -CUDART_INF_F;  // running reference max of this half, log2 units
+    float l = 0.f;                // running row sum of this half
     bool ok = true;
     for (int j = 0; j < nkb && ok; ++j) {
       const int sb = j & 1;
@@ -242,51 +258,47 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sr[HALF];
+      float sv[HALF];
+      {
+        uint32_t* su = reinterpret_cast<uint32_t*>(sv);
 #pragma unroll
-      for (int c = 0; c < HALF / 32; ++c)
-        CFB_TMEM_LD32(lane_addr + sb * BN + half * HALF + c * 32, (sr + c * 32));
+        for (int cc = 0; cc < HALF / 32; ++cc)
+          CFB_TMEM_LD32(lane_addr + sb * BN + half * HALF + cc * 32, (su + cc * 32));
+      }
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
-      // scale, causal mask, partial row max
       const int k0 = j * BN + half * HALF;
-      const bool diag = (k0 + HALF - 1 > q0) || (k0 + HALF > p.S);
+      if ((k0 + HALF - 1 > q0) || (k0 + HALF > p.S)) {  // diagonal / ragged block: mask
+        const int lim = min(qpos, p.S - 1) - k0;      // keys with index <= lim are visible
+#pragma unroll
+        for (int i = 0; i < HALF; ++i)
+          if (i > lim) sv[i] = -CUDART_INF_F;
+      }
       float mx = -CUDART_INF_F;
 #pragma unroll
-      for (int i = 0; i < HALF; ++i) {
-        float v = __uint_as_float(sr[i]) * p.scale_log2;
-        if (diag && (k0 + i > qpos || k0 + i >= p.S)) v = -CUDART_INF_F;
-        sr[i] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
-      }
-      // exchange the partial max with the partner warp
-      float other;
-      ++seq;
-      if (!pair_exchange(red, xflag, 2 * (seq & 1), half, r, seq, mx, other, abort_flag, p.err)) {
-        ok = false;
-        break;
-      }
-      mx = fmaxf(mx, other);
+      for (int i = 0; i < HALF; i += 2) mx = fmax3f(mx, sv[i], sv[i + 1]);
+      mx *= c;  // raw max -> log2 units (c > 0)
       const bool grow = (mx > m_ref + kRescaleThreshold) || (m_ref == -CUDART_INF_F);
       float alpha = 1.f;
       if (grow) {
         const float m_new = fmaxf(m_ref, mx);
-        alpha = (m_ref == -CUDART_INF_F) ? 0.f : exp2f(m_ref - m_new);
+        alpha = (m_ref == -CUDART_INF_F) ? 0.f : ex2_approx(m_ref - m_new);
         m_ref = m_new;
       }
-      const float ref = (m_ref == -CUDART_INF_F) ? 0.f : m_ref;
-      float rs = 0.f;
+      const float nref = (m_ref == -CUDART_INF_F) ? 0.f : -m_ref;
+      float rs0 = 0.f, rs1 = 0.f;
       uint32_t pk[HALF / 2];
 #pragma unroll
       for (int i = 0; i < HALF / 2; ++i) {
-        const float e0 = exp2f(__uint_as_float(sr[2 * i]) - ref);
-        const float e1 = exp2f(__uint_as_float(sr[2 * i + 1]) - ref);
-        rs += e0 + e1;
+        const float e0 = ex2_approx(fmaf(sv[2 * i], c, nref));
+        const float e1 = ex2_approx(fmaf(sv[2 * i + 1], c, nref));
+        rs0 += e0;
+        rs1 += e1;
         pk[i] = pack_bf16x2(e0, e1);
       }
-      l = l * alpha + rs;
+      l = l * alpha + (rs0 + rs1);
       // P_{j-1} V_{j-1} must be complete before P is overwritten and O rescaled
       if (j > 0 &&
           !mbar_wait(smem_u32(o_done), (j - 1) & 1, abort_flag, p.err, kErrWaitSoftmax)) {
@@ -296,13 +308,13 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
 #pragma unroll
-        for (int c = 0; c < OH / 32; ++c) {
+        for (int cc = 0; cc < HD / 32; ++cc) {
           uint32_t o[32];
-          CFB_TMEM_LD32(lane_addr + o_col + half * OH + c * 32, o);
+          CFB_TMEM_LD32(lane_addr + my_o + cc * 32, o);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          CFB_TMEM_ST32(lane_addr + o_col + half * OH + c * 32, o);
+          CFB_TMEM_ST32(lane_addr + my_o + cc * 32, o);
         }
         tmem_st_wait();
       }
@@ -317,34 +329,48 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(p_ready));
     }
-    // epilogue: combine the two partial row sums, O / l, LSE
+    // epilogue: merge the two halves' (m, l, O) once, write O / l and the LSE
     if (ok && mbar_wait(smem_u32(o_done), (nkb - 1) & 1, abort_flag, p.err, kErrWaitSoftmax)) {
       tc_fence_after();
-      float l_other = 0.f;
-      ok = pair_exchange(red, xflag, 4, half, r, ++seq, l, l_other, abort_flag, p.err);
-      const float lt = l + l_other;
-      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
+      volatile int* xflag = reinterpret_cast<volatile int*>(smem + L::OFF_FLAG);
+      float m_o = 0.f, l_o = 0.f;
+      ok = pair_exchange(red, xflag, 0, half, r, 1, m_ref, m_o, abort_flag, p.err) &&
+           pair_exchange(red, xflag, 2, half, r, 2, l, l_o, abort_flag, p.err);
+      const float m0 = half == 0 ? m_ref : m_o, m1 = half == 0 ? m_o : m_ref;
+      const float l0 = half == 0 ? l : l_o, l1 = half == 0 ? l_o : l;
+      const float M = fmaxf(m0, m1);
+      const float f0 = (m0 == -CUDART_INF_F) ? 0.f : ex2_approx(m0 - M);
+      const float f1 = (m1 == -CUDART_INF_F) ? 0.f : ex2_approx(m1 - M);
+      const float Lt = l0 * f0 + l1 * f1;
+      const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
+      const float g0 = f0 * inv, g1 = f1 * inv;
       __nv_bfloat16* dst = p.out + static_cast<long long>(row0 + qpos) * p.ld_out + h * HD + half * OH;
 #pragma unroll
-      for (int c = 0; c < OH / 32; ++c) {
-        uint32_t o[32];
-        CFB_TMEM_LD32(lane_addr + o_col + half * OH + c * 32, o);
+      for (int cc = 0; cc < OH / 32; ++cc) {
+        uint32_t a0[32], a1[32];
+        CFB_TMEM_LD32(lane_addr + o_col + half * OH + cc * 32, a0);
+        CFB_TMEM_LD32(lane_addr + o_col + HD + half * OH + cc * 32, a1);
         tmem_ld_wait();
-        if (qpos < p.S) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+        if (ok && qpos < p.S) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[e] = __uint_as_float(a0[8 * k + e]) * g0 + __uint_as_float(a1[8 * k + e]) * g1;
             uint4 u;
-            u.x = pack_bf16x2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv);
-            u.y = pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv);
-            u.z = pack_bf16x2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv);
-            u.w = pack_bf16x2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv);
+            u.x = pack_bf16x2(v[0], v[1]);
+            u.y = pack_bf16x2(v[2], v[3]);
+            u.z = pack_bf16x2(v[4], v[5]);
+            u.w = pack_bf16x2(v[6], v[7]);
             d4[k] = u;
           }
         }
       }
-      if (qpos < p.S && half == 0)
-        p.lse[static_cast<long long>(row0 + qpos) * p.nh + h] = (m_ref + log2f(lt)) * kLn2;
+      if (ok && qpos < p.S && half == 0)
+        p.lse[static_cast<long long>(row0 + qpos) * p.nh + h] = (M + log2f(Lt)) * kLn2;
     }
   }
 
