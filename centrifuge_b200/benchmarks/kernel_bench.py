@@ -83,6 +83,14 @@ def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3
         fl = 4.0 * B * nh * hd * (Sk * Sk / 2) + 6.0 * B * nh * hd * (Sk * S / 2)
         res.append({"name": f"attn_bwd_keep{keep}", "Sk": Sk, "ms": ms, "tflops": fl / ms / 1e9})
         print(json.dumps(res[-1]))
+        if keep == keeps[0]:
+            delta = torch.empty(B * Sk * nh, dtype=torch.float32, device="cuda")
+            ms_m = _time(lambda: kernels().attn_bwd_mma(qkv_k, qkv, o_k, do_k, lse_k,
+                                                        pos.reshape(-1), dq, delta, B, S, Sk, nh,
+                                                        nkv, hd, 1.0 / hd ** 0.5), iters=10)
+            res.append({"name": f"attn_bwd_mma_sync_keep{keep}", "Sk": Sk, "ms": ms_m,
+                        "tflops": fl / ms_m / 1e9})
+            print(json.dumps(res[-1]))
     return res
 
 

@@ -348,9 +348,10 @@ void attn_fwd(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S,
                "attn_fwd");
 }
 
-void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, const Tensor& do_k,
-              const Tensor& lse_k, const Tensor& pos_k, Tensor& dqkv_k, Tensor& delta, int64_t B,
-              int64_t S, int64_t Sk, int64_t nh, int64_t nkv, int64_t hd, double scale) {
+void check_attn_bwd_args(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k,
+                         const Tensor& do_k, const Tensor& lse_k, const Tensor& pos_k,
+                         const Tensor& dqkv_k, const Tensor& delta, int64_t B, int64_t S,
+                         int64_t Sk, int64_t nh) {
   check_bf16_2d(qkv_k, "qkv_k");
   check_bf16_2d(qkv_full, "qkv_full");
   check_bf16_2d(o_k, "o_k");
@@ -363,13 +364,38 @@ void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, co
   TORCH_CHECK(pos_k.scalar_type() == at::kInt && pos_k.numel() == B * Sk, "pos_k int32");
   TORCH_CHECK(delta.scalar_type() == at::kFloat && delta.numel() >= B * Sk * nh, "delta");
   TORCH_CHECK(lse_k.scalar_type() == at::kFloat && lse_k.numel() == B * Sk * nh, "lse_k");
+}
+
+// Filtered causal GQA attention backward on tcgen05/TMEM (the production path).
+void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, const Tensor& do_k,
+              const Tensor& lse_k, const Tensor& pos_k, Tensor& dqkv_k, Tensor& delta, int64_t B,
+              int64_t S, int64_t Sk, int64_t nh, int64_t nkv, int64_t hd, double scale) {
+  check_attn_bwd_args(qkv_k, qkv_full, o_k, do_k, lse_k, pos_k, dqkv_k, delta, B, S, Sk, nh);
+  const c10::cuda::CUDAGuard guard(qkv_k.device());
+  CFB_CHECK_RC(cfb_attn_delta(o_k.data_ptr(), do_k.data_ptr(), o_k.stride(0),
+                              delta.data_ptr<float>(), B * Sk, nh, hd, cur_stream()),
+               "attn_delta");
+  CFB_CHECK_RC(cfb_attn_bwd_tc(qkv_k.data_ptr(), qkv_k.stride(0), qkv_full.data_ptr(),
+                               do_k.data_ptr(), do_k.stride(0), lse_k.data_ptr<float>(),
+                               delta.data_ptr<float>(), pos_k.data_ptr<int>(), dqkv_k.data_ptr(),
+                               B, S, Sk, nh, nkv, hd, scale,
+                               err_word(qkv_k.get_device()).data_ptr<int>(), cur_stream()),
+               "attn_bwd");
+}
+
+// mma.sync (legacy tensor path) backward, kept as a comparison point.
+void attn_bwd_mma(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k,
+                  const Tensor& do_k, const Tensor& lse_k, const Tensor& pos_k, Tensor& dqkv_k,
+                  Tensor& delta, int64_t B, int64_t S, int64_t Sk, int64_t nh, int64_t nkv,
+                  int64_t hd, double scale) {
+  check_attn_bwd_args(qkv_k, qkv_full, o_k, do_k, lse_k, pos_k, dqkv_k, delta, B, S, Sk, nh);
   const c10::cuda::CUDAGuard guard(qkv_k.device());
   CFB_CHECK_RC(cfb_attn_bwd(qkv_k.data_ptr(), qkv_k.stride(0), qkv_full.data_ptr(),
                             o_k.data_ptr(), o_k.stride(0), do_k.data_ptr(),
                             lse_k.data_ptr<float>(), pos_k.data_ptr<int>(), dqkv_k.data_ptr(),
                             nullptr, delta.data_ptr<float>(), B, S, Sk, nh, nkv, hd, scale,
                             cur_stream()),
-               "attn_bwd");
+               "attn_bwd_mma");
 }
 
 // ---- NVLink peer-memory gradient reduction (pointers are raw device addresses from the
@@ -460,6 +486,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_fwd_mma", &attn_fwd_mma);
   m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd_mma", &attn_bwd_mma);
   m.def("symm_signal", &symm_signal);
   m.def("symm_wait", &symm_wait);
   m.def("symm_pull_reduce", &symm_pull_reduce);

@@ -606,3 +606,12 @@ int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, cons
                                       dqkv_k, delta, B, S, Sk, nh, nkv, scale, st);
   return -12;
 }
+
+int cfb_attn_delta(const void* o_k, const void* do_k, long long ld_o, float* delta, long long rows,
+                   int nh, int hd, cudaStream_t st) {
+  if (ld_o % 8 || hd % 8) return -11;
+  cfb::attn::attn_delta_kernel<<<static_cast<int>((rows * nh + 255) / 256), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(o_k), static_cast<const __nv_bfloat16*>(do_k), ld_o,
+      delta, static_cast<int>(rows), nh, hd);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}

@@ -174,7 +174,8 @@ __global__ void __launch_bounds__(320, 1)
       for (int c = 0; c < HD / 64; ++c)
         tma_load_2d(sbase + L::OFF_Q + c * L::CHUNK, &tm, smem_u32(q_full), qcol + c * 64,
                     row0 + q0);
-      for (int j = 0; j < nkb; ++j) {
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j, ++issued) {
         const int st = j % KV_STAGES;
         if (!mbar_wait(smem_u32(&kv_empty[st]), ((j / KV_STAGES) & 1) ^ 1, abort_flag, p.err,
                        kErrWaitProducer))
@@ -188,6 +189,8 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_2d(sbase + L::OFF_V + st * L::KV_TILE + c * L::CHUNK, &tm, fb, vcol + c * 64, k0);
         }
       }
+      tma_drain_ring(kv_full, KV_STAGES, issued);
+      tma_drain_ring(q_full, 1, 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {

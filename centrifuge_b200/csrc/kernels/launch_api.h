@@ -64,6 +64,16 @@ int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, cons
                  void* dqkv_k, float* unused, float* delta, int B, int S, int Sk, int nh,
                  int nkv, int hd, float scale, cudaStream_t st);
 
+// delta[r, h] = <O[r, h, :], dO[r, h, :]> over the kept rows (attention backward prologue).
+int cfb_attn_delta(const void* o_k, const void* do_k, long long ld_o, float* delta, long long rows,
+                   int nh, int hd, cudaStream_t st);
+// tcgen05/TMEM filtered backward (attention_bwd_sm100.cu): dK/dV of the kept keys and dQ of the
+// kept queries over all keys by position; `delta` must be computed first.
+int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, const void* do_k,
+                    long long ld_o, const float* lse_k, const float* delta, const int* pos_k,
+                    void* dqkv_k, int B, int S, int Sk, int nh, int nkv, int hd, float scale,
+                    int* err, cudaStream_t st);
+
 // NVLink peer-memory gradient reduction (comm_sm100.cu).
 int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,
                     cudaStream_t st);

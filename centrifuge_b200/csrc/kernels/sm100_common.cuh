@@ -85,6 +85,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Producer exit: wait (bounded, not abortable) until the copies issued into a ring of
+// `stages` buffers (`issued` fills in total, fill i into buffer i % stages, completion on
+// full[i % stages]) have landed, so that no TMA write reaches shared memory after the CTA has
+// given up and exited.  On the normal path every wait returns at once.
+__device__ __forceinline__ void tma_drain_ring(uint64_t* full, int stages, int issued) {
+  volatile int no_abort = 0;
+  for (int st = 0; st < stages; ++st) {
+    const int last = issued - 1 - (((issued - 1 - st) % stages) + stages) % stages;
+    if (last >= 0) mbar_wait(smem_u32(&full[st]), (last / stages) & 1, &no_abort, nullptr, 0);
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -199,7 +199,9 @@ def test_attention_fwd(B, S, nh, nkv, hd):
 
 
 @pytest.mark.parametrize("B,S,nh,nkv,hd,keep", [(2, 256, 4, 2, 64, 0.5), (1, 320, 4, 1, 128, 0.3),
-                                                (2, 256, 8, 2, 128, 1.0), (1, 128, 2, 2, 64, 0.7)])
+                                                (2, 256, 8, 2, 128, 1.0), (1, 128, 2, 2, 64, 0.7),
+                                                (2, 1024, 8, 2, 128, 0.5), (1, 700, 4, 4, 64, 0.6),
+                                                (2, 2048, 4, 1, 64, 0.5), (1, 96, 2, 1, 128, 0.9)])
 def test_attention_bwd_filtered(B, S, nh, nkv, hd, keep):
     torch.manual_seed(10)
     ld = (nh + 2 * nkv) * hd
@@ -224,3 +226,11 @@ def test_attention_bwd_filtered(B, S, nh, nkv, hd, keep):
     assert rel_err(d[:, : nh * hd], dq.reshape(B * Sk, -1)) < 2e-2
     assert rel_err(d[:, nh * hd:(nh + nkv) * hd], dk.reshape(B * Sk, -1)) < 2e-2
     assert rel_err(d[:, (nh + nkv) * hd:], dv.reshape(B * Sk, -1)) < 2e-2
+    from centrifuge_b200.ops import kernels
+    assert kernels().gemm_error_word(0, True) == 0
+    # the warp-level mma.sync backward agrees too
+    d2 = torch.empty_like(d)
+    delta = torch.empty(B * Sk * nh, dtype=torch.float32, device=dev)
+    kernels().attn_bwd_mma(qkv_k, qkv, o_k, do_k, lse_k, pos.reshape(-1), d2, delta, B, S, Sk, nh,
+                           nkv, hd, 1.0 / hd ** 0.5)
+    assert rel_err(d2, d) < 2e-2
