@@ -101,6 +101,8 @@ def main():
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--attn-shape", default="4,4096,32,8,128",
                     help="B,S,nh,nkv,hd of the attention benchmark")
+    ap.add_argument("--keeps", default="1.0,0.7,0.5,0.3",
+                    help="kept fractions of the filtered attention backward benchmark")
     args = ap.parse_args()
     shapes = [
         (8192, 8192, 8192, False, False, "square"),
@@ -116,7 +118,8 @@ def main():
         out["gemm"] = bench_gemm(shapes)
     if not args.skip_attn:
         B, S, nh, nkv, hd = (int(x) for x in args.attn_shape.split(","))
-        out["attention"] = bench_attention(B, S, nh, nkv, hd)
+        keeps = tuple(float(x) for x in args.keeps.split(","))
+        out["attention"] = bench_attention(B, S, nh, nkv, hd, keeps=keeps)
     if args.json:
         with open(args.json, "w") as f:
             json.dump(out, f, indent=1)

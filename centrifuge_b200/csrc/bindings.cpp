@@ -38,6 +38,15 @@ Tensor& err_word(int device) {
   return w;
 }
 
+// Work counter of the persistent attention backward (two int32 words per device, zero at rest).
+Tensor& attn_work_counter(int device) {
+  static std::vector<Tensor> words(64);
+  Tensor& w = words.at(device);
+  if (!w.defined())
+    w = at::zeros({2}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+  return w;
+}
+
 // out[M, N] = epi(alpha * op(a) @ op(b))
 //   a: [M, K] (a_mn = false) or [K, M] (a_mn = true)
 //   b: [N, K] (b_mn = false) or [K, N] (b_mn = true)
@@ -379,6 +388,7 @@ void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, co
                                do_k.data_ptr(), do_k.stride(0), lse_k.data_ptr<float>(),
                                delta.data_ptr<float>(), pos_k.data_ptr<int>(), dqkv_k.data_ptr(),
                                B, S, Sk, nh, nkv, hd, scale,
+                               attn_work_counter(qkv_k.get_device()).data_ptr<int>(),
                                err_word(qkv_k.get_device()).data_ptr<int>(), cur_stream()),
                "attn_bwd");
 }

@@ -68,11 +68,13 @@ int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, cons
 int cfb_attn_delta(const void* o_k, const void* do_k, long long ld_o, float* delta, long long rows,
                    int nh, int hd, cudaStream_t st);
 // tcgen05/TMEM filtered backward (attention_bwd_sm100.cu): dK/dV of the kept keys and dQ of the
-// kept queries over all keys by position; `delta` must be computed first.
+// kept queries over all keys by position; `delta` must be computed first.  Persistent kernel
+// scheduled through `work` (two device int32 words, zero before the first launch; the kernel
+// leaves them zero).  Launches sharing one `work` pair must be ordered (one stream).
 int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, const void* do_k,
                     long long ld_o, const float* lse_k, const float* delta, const int* pos_k,
                     void* dqkv_k, int B, int S, int Sk, int nh, int nkv, int hd, float scale,
-                    int* err, cudaStream_t st);
+                    int* work, int* err, cudaStream_t st);
 
 // NVLink peer-memory gradient reduction (comm_sm100.cu).
 int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,
