@@ -38,7 +38,8 @@ Tensor& err_word(int device) {
   return w;
 }
 
-// Work counter of the persistent attention backward (two int32 words per device, zero at rest).
+// Work counter of the persistent attention kernels (two int32 words per device, zero at rest;
+// forward and backward launches on one device are stream-ordered, so they share it).
 Tensor& attn_work_counter(int device) {
   static std::vector<Tensor> words(64);
   Tensor& w = words.at(device);
@@ -353,6 +354,7 @@ void attn_fwd(const Tensor& qkv, Tensor& out, Tensor& lse, int64_t B, int64_t S,
   const c10::cuda::CUDAGuard guard(qkv.device());
   CFB_CHECK_RC(cfb_attn_fwd_tc(qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0),
                                lse.data_ptr<float>(), B, S, nh, nkv, hd, scale,
+                               attn_work_counter(qkv.get_device()).data_ptr<int>(),
                                err_word(qkv.get_device()).data_ptr<int>(), cur_stream()),
                "attn_fwd");
 }

@@ -56,8 +56,10 @@ int cfb_scale_f32(float* x, long long n, float s, cudaStream_t st);
 int cfb_attn_fwd(const void* qkv, long long ld_qkv, void* out, long long ld_out, float* lse,
                  int B, int S, int nh, int nkv, int hd, float scale, cudaStream_t st);
 // tcgen05/TMEM forward (attention_sm100.cu); `err` receives a code if a bounded wait gives up.
+// Persistent kernel scheduled through `work` (two device int32 words, zero before the first
+// launch; the kernel leaves them zero).  Launches sharing one `work` pair must be ordered.
 int cfb_attn_fwd_tc(const void* qkv, long long ld_qkv, void* out, long long ld_out, float* lse,
-                    int B, int S, int nh, int nkv, int hd, float scale, int* err,
+                    int B, int S, int nh, int nkv, int hd, float scale, int* work, int* err,
                     cudaStream_t st);
 int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, const void* o_k,
                  long long ld_o, const void* do_k, const float* lse_k, const int* pos_k,
