@@ -15,9 +15,10 @@
 //                             (O0, O1 in TMEM, fed by two K=64 PV MMAs), so the halves never
 //                             synchronise per step; the epilogue merges them once
 //                             (O = O0 2^(m0-m) + O1 2^(m1-m), same for l).  Online softmax in
-//                             fp32 with one FMA + ex2 per score, P written to shared memory as
-//                             bf16 (128B-swizzled K-major operand); a running max only moves
-//                             (and its O is rescaled in TMEM) when it grows by more than 2^8
+//                             fp32 with one FMA + ex2 per score; P (bf16) is written back into
+//                             TMEM over the thread's own S columns and feeds P V as the TMEM A
+//                             operand, so P never touches shared memory; a running max only
+//                             moves (and its O is rescaled in TMEM) when it grows by more than 2^8
 // S_{j+1} is issued before P_j V_j so that the tensor cores compute the next scores while the
 // softmax warps work on the current ones, and the next item's first scores overlap this item's
 // epilogue.  Q, K and V are read straight from the fused [T, (nh + 2 nkv) hd] qkv rows with one
@@ -37,21 +38,19 @@ constexpr int BM = 128, BN = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
-constexpr int MAX_RING = 3;
+constexpr int MAX_RING = 4;
 
 template <int HD>
 struct Smem {
   static constexpr int QBUF = HD == 64 ? 2 : 1;           // Q buffers (items in flight)
-  static constexpr int KV_STAGES = HD == 64 ? 3 : 2;      // slots of each of the K and V rings
+  static constexpr int KV_STAGES = HD == 64 ? 4 : 2;      // slots of each of the K and V rings
   static constexpr int CHUNK = BM * 128;                  // 128 rows x 128 B (64 bf16)
   static constexpr int Q_BYTES = (HD / 64) * CHUNK;       // Q [128 x HD], K-major chunks
   static constexpr int KV_TILE = (HD / 64) * CHUNK;       // K_j or V_j [128 x HD]
-  static constexpr int P_BYTES = 2 * CHUNK;               // P [128 x 128 keys], 2 K-chunks
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QBUF * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KV_STAGES * KV_TILE;
-  static constexpr int OFF_P = OFF_V + KV_STAGES * KV_TILE;
-  static constexpr int OFF_RED = OFF_P + P_BYTES;  // epilogue exchange: [4 slots][128] fp32
+  static constexpr int OFF_RED = OFF_V + KV_STAGES * KV_TILE;  // epilogue exchange: [4][128] fp32
   static constexpr int OFF_FLAG = OFF_RED + 4 * BM * 4;  // [2 half][128] exchange counters
   static constexpr int OFF_BAR = OFF_FLAG + 2 * BM * 4;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;     // + barriers + alignment slack
@@ -289,12 +288,14 @@ __global__ void __launch_bounds__(320, 1)
               !mbar_wait(smem_u32(&bar->s_free[sb]), (use - 1) & 1, abort_flag, p.err, kErrWaitMma))
             return false;
           tc_fence_after();
-          const uint32_t kst = sbase + L::OFF_K + st * L::KV_TILE;
+          // descriptors of consecutive K steps differ only in the start-address field
+          const uint64_t qd = sdesc_sw128(sq, 16, 1024);
+          const uint64_t kd = sdesc_sw128(sbase + L::OFF_K + st * L::KV_TILE, 16, 1024);
+          const uint32_t dst = tmem + sb * BN;
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * L::CHUNK + (kk & 3) * 32;
-            umma_bf16_ss(tmem + sb * BN, sdesc_sw128(sq + off, 16, 1024),
-                         sdesc_sw128(kst + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+            const uint32_t off = ((kk >> 2) * L::CHUNK + (kk & 3) * 32) >> 4;
+            umma_bf16_ss(dst, qd + off, kd + off, IDESC_S, kk > 0 ? 1u : 0u);
           }
           umma_commit(smem_u32(&bar->s_full[sb]));
           umma_commit(smem_u32(&bar->k_empty[st]));
@@ -310,15 +311,16 @@ __global__ void __launch_bounds__(320, 1)
           if (!mbar_wait(smem_u32(&bar->p_ready), gg & 1, abort_flag, p.err, kErrWaitMma))
             return false;
           tc_fence_after();
-          const uint32_t vst = sbase + L::OFF_V + st * L::KV_TILE;
+          const uint64_t vd = sdesc_sw128(sbase + L::OFF_V + st * L::KV_TILE, L::CHUNK, 1024);
+          const uint32_t pa = tmem + (gg & 1) * BN;
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            // keys [0, 64) accumulate into O0, keys [64, 128) into O1
+            // keys [0, 64) accumulate into O0, keys [64, 128) into O1; P_j (bf16) sits in the
+            // first 32 columns of each half of S_j's TMEM tile
             const int hh = kk >> 2;
-            const uint32_t aoff = hh * L::CHUNK + (kk & 3) * 32;
-            umma_bf16_ss(tmem + o_col + hh * HD, sdesc_sw128(sbase + L::OFF_P + aoff, 16, 1024),
-                         sdesc_sw128(vst + kk * 2048, L::CHUNK, 1024), IDESC_O,
-                         (j > 0 || (kk & 3) > 0) ? 1u : 0u);
+            umma_bf16_ts(tmem + o_col + hh * HD, pa + hh * 64 + (kk & 3) * 8,
+                         vd + ((kk * 2048) >> 4), IDESC_O, (kk & 3) > 0 ? 1u : acc0);
           }
           umma_commit(smem_u32(&bar->o_done));
           umma_commit(smem_u32(&bar->v_empty[st]));
@@ -388,9 +390,13 @@ __global__ void __launch_bounds__(320, 1)
           for (int i = 0; i < HALF; ++i)
             if (i > lim) sv[i] = -CUDART_INF_F;
         }
-        float mx = -CUDART_INF_F;
+        float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-        for (int i = 0; i < HALF; i += 2) mx = fmax3f(mx, sv[i], sv[i + 1]);
+        for (int i = 0; i < HALF; i += 8) {  // four independent max chains
+#pragma unroll
+          for (int q = 0; q < 4; ++q) m4[q] = fmax3f(m4[q], sv[i + 2 * q], sv[i + 2 * q + 1]);
+        }
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
         mx *= c;  // raw max -> log2 units (c > 0)
         const bool grow = (mx > m_ref + kRescaleThreshold) || (m_ref == -CUDART_INF_F);
         float alpha = 1.f;
@@ -400,25 +406,29 @@ __global__ void __launch_bounds__(320, 1)
           m_ref = m_new;
         }
         const float nref = (m_ref == -CUDART_INF_F) ? 0.f : -m_ref;
-        float rs0 = 0.f, rs1 = 0.f;
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
         uint32_t pk[HALF / 2];
 #pragma unroll
         for (int i = 0; i < HALF / 2; ++i) {
           const float e0 = ex2_approx(fmaf(sv[2 * i], c, nref));
           const float e1 = ex2_approx(fmaf(sv[2 * i + 1], c, nref));
-          rs0 += e0;
-          rs1 += e1;
+          rs[(2 * i) & 3] += e0;
+          rs[(2 * i + 1) & 3] += e1;
           pk[i] = pack_bf16x2(e0, e1);
         }
-        l = l * alpha + (rs0 + rs1);
-        // P_{j-1} V_{j-1} must be complete before P is overwritten and O rescaled
+        l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        // P_{j-1} V_{j-1} must be complete before P_j is written to TMEM (and before O is
+        // rescaled).  Writing P_j while that MMA was still in flight corrupted rows of O on
+        // B200, although P_j and P_{j-1} occupy different TMEM columns.
         if (gg > 0 &&
             !mbar_wait(smem_u32(&bar->o_done), (gg - 1) & 1, abort_flag, p.err, kErrWaitSoftmax)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // P_j (bf16, 32 columns) overwrites the first half of this thread's own 64 S columns
+        CFB_TMEM_ST32(lane_addr + sb * BN + half * HALF, pk);
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {  // a grown max rescales this half's O
 #pragma unroll
           for (int cc = 0; cc < HD / 32; ++cc) {
             uint32_t o[32];
@@ -428,15 +438,8 @@ __global__ void __launch_bounds__(320, 1)
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             CFB_TMEM_ST32(lane_addr + my_o + cc * 32, o);
           }
-          tmem_st_wait();
         }
-        // this thread's 64 keys of the P row = K-chunk `half` of the PV operand (128B swizzle)
-        const uint32_t rowbase = sbase + L::OFF_P + half * L::CHUNK + r * 128;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          st_shared_v4(rowbase + ((i ^ (r & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2],
-                       pk[4 * i + 3]);
-        fence_async_shared();
+        tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&bar->p_ready));

@@ -198,6 +198,31 @@ def test_attention_fwd(B, S, nh, nkv, hd):
     assert rel_err(o2, o) < 1e-2 and rel_err(l2, lse) < 1e-4
 
 
+@pytest.mark.parametrize("B,S,nh,nkv,hd,amp", [(8, 2048, 32, 4, 64, 1.0), (4, 2048, 32, 8, 128, 1.0),
+                                               (8, 1024, 32, 4, 64, 4.0)])
+def test_attention_fwd_many_items(B, S, nh, nkv, hd, amp):
+    """More work items than SMs: the persistent kernel runs several items per CTA.  Compared
+    element-wise against the warp-level mma.sync forward."""
+    from centrifuge_b200.ops import kernels
+    torch.manual_seed(11)
+    ld = (nh + 2 * nkv) * hd
+    qkv = (amp * torch.randn(B * S, ld, device=dev)).bfloat16()
+    o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
+    o2, l2 = torch.empty_like(o), torch.empty_like(lse)
+    kernels().attn_fwd_mma(qkv, o2, l2, B, S, nh, nkv, hd, 1.0 / hd ** 0.5)
+    assert kernels().gemm_error_word(0, True) == 0
+    assert (lse - l2).abs().max().item() < 1e-3
+    # against the fp32 oracle, the tcgen05 kernel is as accurate as the mma.sync one
+    q = qkv[:, : nh * hd].reshape(B, S, nh, hd)
+    k = qkv[:, nh * hd:(nh + nkv) * hd].reshape(B, S, nkv, hd)
+    v = qkv[:, (nh + nkv) * hd:].reshape(B, S, nkv, hd)
+    orf, _ = ref.attention(q, k, v)
+    orf = orf.reshape(B * S, nh * hd)
+    e_tc = (o.float() - orf).abs().max().item()
+    e_mma = (o2.float() - orf).abs().max().item()
+    assert e_tc <= 1.5 * e_mma + 1e-2, (e_tc, e_mma)
+
+
 @pytest.mark.parametrize("B,S,nh,nkv,hd,keep", [(2, 256, 4, 2, 64, 0.5), (1, 320, 4, 1, 128, 0.3),
                                                 (2, 256, 8, 2, 128, 1.0), (1, 128, 2, 2, 64, 0.7),
                                                 (2, 1024, 8, 2, 128, 0.5), (1, 700, 4, 4, 64, 0.6),
