@@ -94,6 +94,32 @@ void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool a_mn, bool b_mn, i
   CFB_CHECK_RC(rc, "gemm");
 }
 
+// out[M, N] = a @ b^T (both K-major) with rotate-half RoPE applied in the epilogue to columns
+// [0, rope_cols) (heads of hd columns) at positions pos[M] (int32), table [max_pos, hd/2, 2] fp32.
+void gemm_rope(const Tensor& a, const Tensor& b, Tensor& out, const Tensor& pos,
+               const Tensor& table, int64_t rope_cols, int64_t hd, int64_t bn) {
+  check_bf16_2d(a, "a");
+  check_bf16_2d(b, "b");
+  check_bf16_2d(out, "out");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K, "gemm_rope: inner dimensions differ");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_rope: out shape");
+  TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == at::kInt && pos.numel() == M &&
+                  pos.is_contiguous(), "gemm_rope: pos must be int32 [M] on the device");
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kFloat && table.is_contiguous() &&
+                  table.dim() == 3 && table.size(1) == hd / 2 && table.size(2) == 2,
+              "gemm_rope: table must be fp32 [max_pos, hd/2, 2]");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  CFB_CHECK_RC(cfb_gemm_bf16_rope(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
+                                  out.data_ptr(), out.stride(0), static_cast<int>(M),
+                                  static_cast<int>(N), static_cast<int>(K), pos.data_ptr<int>(),
+                                  table.data_ptr<float>(), static_cast<int>(rope_cols),
+                                  static_cast<int>(hd), err_word(a.get_device()).data_ptr<int>(),
+                                  static_cast<int>(bn), 0, cur_stream()),
+               "gemm_rope");
+}
+
 int64_t gemm_error_word(int64_t device, bool reset) {
   Tensor& w = err_word(static_cast<int>(device));
   const int64_t v = w.item<int>();
@@ -380,8 +406,17 @@ void check_attn_bwd_args(const Tensor& qkv_k, const Tensor& qkv_full, const Tens
 // Filtered causal GQA attention backward on tcgen05/TMEM (the production path).
 void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, const Tensor& do_k,
               const Tensor& lse_k, const Tensor& pos_k, Tensor& dqkv_k, Tensor& delta, int64_t B,
-              int64_t S, int64_t Sk, int64_t nh, int64_t nkv, int64_t hd, double scale) {
+              int64_t S, int64_t Sk, int64_t nh, int64_t nkv, int64_t hd, double scale,
+              const c10::optional<Tensor>& rope_table) {
   check_attn_bwd_args(qkv_k, qkv_full, o_k, do_k, lse_k, pos_k, dqkv_k, delta, B, S, Sk, nh);
+  const float* cs = nullptr;
+  if (rope_table.has_value() && rope_table->defined()) {
+    const Tensor& t = *rope_table;
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() &&
+                    t.dim() == 3 && t.size(1) == hd / 2 && t.size(2) == 2 && t.size(0) >= S,
+                "attn_bwd: rope_table must be fp32 [max_pos >= S, hd/2, 2]");
+    cs = t.data_ptr<float>();
+  }
   const c10::cuda::CUDAGuard guard(qkv_k.device());
   CFB_CHECK_RC(cfb_attn_delta(o_k.data_ptr(), do_k.data_ptr(), o_k.stride(0),
                               delta.data_ptr<float>(), B * Sk, nh, hd, cur_stream()),
@@ -389,7 +424,7 @@ void attn_bwd(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& o_k, co
   CFB_CHECK_RC(cfb_attn_bwd_tc(qkv_k.data_ptr(), qkv_k.stride(0), qkv_full.data_ptr(),
                                do_k.data_ptr(), do_k.stride(0), lse_k.data_ptr<float>(),
                                delta.data_ptr<float>(), pos_k.data_ptr<int>(), dqkv_k.data_ptr(),
-                               B, S, Sk, nh, nkv, hd, scale,
+                               B, S, Sk, nh, nkv, hd, scale, cs,
                                attn_work_counter(qkv_k.get_device()).data_ptr<int>(),
                                err_word(qkv_k.get_device()).data_ptr<int>(), cur_stream()),
                "attn_bwd");
@@ -452,7 +487,8 @@ Tensor attn_bwd_rows(const Tensor& qkv_k, const Tensor& qkv_full, const Tensor& 
   Tensor dqkv = at::empty_like(qkv_k);
   Tensor delta = at::empty({B * Sk * nh}, qkv_k.options().dtype(at::kFloat));
   Tensor o = o_k.contiguous(), d = do_k.contiguous();
-  attn_bwd(qkv_k, qkv_full, o, d, lse_k, pos_k, dqkv, delta, B, S, Sk, nh, nkv, hd, scale);
+  attn_bwd(qkv_k, qkv_full, o, d, lse_k, pos_k, dqkv, delta, B, S, Sk, nh, nkv, hd, scale,
+           c10::nullopt);
   return dqkv;
 }
 
@@ -476,6 +512,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("resid") = py::none(),
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
+  m.def("gemm_rope", &gemm_rope, "tcgen05 bf16 GEMM with RoPE fused into the epilogue",
+        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("pos"), py::arg("table"),
+        py::arg("rope_cols"), py::arg("hd"), py::arg("bn") = 0);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rope", &rope);
@@ -497,7 +536,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_f32", &scale_f32);
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_fwd_mma", &attn_fwd_mma);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd", &attn_bwd, py::arg("qkv_k"), py::arg("qkv_full"), py::arg("o_k"),
+        py::arg("do_k"), py::arg("lse_k"), py::arg("pos_k"), py::arg("dqkv_k"), py::arg("delta"),
+        py::arg("B"), py::arg("S"), py::arg("Sk"), py::arg("nh"), py::arg("nkv"), py::arg("hd"),
+        py::arg("scale"), py::arg("rope_table") = py::none());
   m.def("attn_bwd_mma", &attn_bwd_mma);
   m.def("symm_signal", &symm_signal);
   m.def("symm_wait", &symm_wait);

@@ -19,6 +19,9 @@
 // dQ += dS K in TMEM.  Dropped keys therefore contribute to dQ exactly as in the reference's
 // second (restore-Q) backward, in one pass and without a bias tensor.
 //
+// With a RoPE table the dQ and dK epilogues also apply the RoPE backward (rotation by the negated
+// angle of the row's position), so no separate pass runs over dqkv.
+//
 // Persistent kernel: one CTA per SM takes items from a global counter (heaviest first: dK/dV
 // items by ascending key block, then dQ items by descending query block).  The A/B tiles of an
 // item (K,V or Q,dO) are double-buffered so the next item's tiles load while the current one
@@ -82,6 +85,8 @@ struct Params {
   long long ld;
   int* work;           // [2]: next item, finished CTAs (zero between launches)
   int* err;
+  const float* cs;     // optional RoPE table [max_pos, HD/2, 2] (cos, sin): dQ and dK leave
+                       // rotated back by -angle(position) (the RoPE backward), else nullptr
 };
 
 struct Bars {
@@ -148,6 +153,49 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t* 
     a.z = pack_bf16x2(__uint_as_float(v[8 * k + 4]) * mul, __uint_as_float(v[8 * k + 5]) * mul);
     a.w = pack_bf16x2(__uint_as_float(v[8 * k + 6]) * mul, __uint_as_float(v[8 * k + 7]) * mul);
     d4[k] = a;
+  }
+}
+
+// Epilogue of dQ or dK: the thread (TMEM lane = row, `half` of the epilogue pair) owns columns
+// [i0, i0 + HD/4) and [HD/2 + i0, HD/2 + i0 + HD/4) with i0 = half * HD/4, i.e. both members of
+// every rotate-half pair it stores.  Scaled by `mul`; with a table, rotated by -angle(pos).
+template <int HD>
+__device__ __forceinline__ void store_rot_pairs(uint32_t t_acc, __nv_bfloat16* head_dst, int half,
+                                                float mul, const float* cs, int pos, bool valid) {
+  constexpr int Q4 = HD / 4, H2 = HD / 2;
+  const int i0 = half * Q4;
+  uint32_t a[Q4], b[Q4];
+  if constexpr (Q4 == 32) {
+    CFB_TMEM_LD32(t_acc + i0, a);
+    CFB_TMEM_LD32(t_acc + H2 + i0, b);
+  } else {
+    CFB_TMEM_LD16(t_acc + i0, a);
+    CFB_TMEM_LD16(t_acc + H2 + i0, b);
+  }
+  tmem_ld_wait();
+  if (!valid) return;
+  uint32_t oa[Q4 / 2], ob[Q4 / 2];
+  const float2* c2 = cs ? reinterpret_cast<const float2*>(cs) + static_cast<long long>(pos) * H2 + i0
+                        : nullptr;
+#pragma unroll
+  for (int t = 0; t < Q4 / 2; ++t) {
+    float x0 = __uint_as_float(a[2 * t]) * mul, x1 = __uint_as_float(a[2 * t + 1]) * mul;
+    float y0 = __uint_as_float(b[2 * t]) * mul, y1 = __uint_as_float(b[2 * t + 1]) * mul;
+    if (c2) {
+      const float2 q0 = __ldg(c2 + 2 * t), q1 = __ldg(c2 + 2 * t + 1);
+      const float rx0 = x0 * q0.x + y0 * q0.y, ry0 = y0 * q0.x - x0 * q0.y;
+      const float rx1 = x1 * q1.x + y1 * q1.y, ry1 = y1 * q1.x - x1 * q1.y;
+      x0 = rx0; y0 = ry0; x1 = rx1; y1 = ry1;
+    }
+    oa[t] = pack_bf16x2(x0, x1);
+    ob[t] = pack_bf16x2(y0, y1);
+  }
+  uint4* da = reinterpret_cast<uint4*>(head_dst + i0);
+  uint4* db = reinterpret_cast<uint4*>(head_dst + H2 + i0);
+#pragma unroll
+  for (int j = 0; j < Q4 / 8; ++j) {
+    da[j] = make_uint4(oa[4 * j], oa[4 * j + 1], oa[4 * j + 2], oa[4 * j + 3]);
+    db[j] = make_uint4(ob[4 * j], ob[4 * j + 1], ob[4 * j + 2], ob[4 * j + 3]);
   }
 }
 
@@ -451,17 +499,17 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(smem_u32(&bar->mm_done), gl & 1, abort_flag, p.err, kErrWaitSoftmax)) break;
         tc_fence_after();
         const int kcol = (p.nh + t.head) * HD, vcol = (p.nh + p.nkv + t.head) * HD;
-        __nv_bfloat16* drow = p.dqkv + static_cast<long long>(rowk + min(kc, p.Sk - 1)) * p.ld;
+        const bool kvalid = kc < p.Sk;
+        const long long krow = static_cast<long long>(rowk + min(kc, p.Sk - 1));
+        __nv_bfloat16* drow = p.dqkv + krow * p.ld;
+        store_rot_pairs<HD>(lane_addr + kColAcc, drow + kcol, half, p.scale, p.cs,
+                            kvalid ? __ldg(p.pos_k + krow) : 0, kvalid);
 #pragma unroll
         for (int cc = 0; cc < OH / 32; ++cc) {
-          uint32_t dk[32], dv[32];
-          CFB_TMEM_LD32(lane_addr + kColAcc + half * OH + cc * 32, dk);
+          uint32_t dv[32];
           CFB_TMEM_LD32(lane_addr + kColAcc + HD + half * OH + cc * 32, dv);
           tmem_ld_wait();
-          if (kc < p.Sk) {
-            store_row32(drow + kcol + half * OH + cc * 32, dk, p.scale);
-            store_row32(drow + vcol + half * OH + cc * 32, dv, 1.f);
-          }
+          if (kvalid) store_row32(drow + vcol + half * OH + cc * 32, dv, 1.f);
         }
       } else {
         const int qc = t.blk * BR + r;  // compact query of this row
@@ -514,14 +562,8 @@ __global__ void __launch_bounds__(320, 1)
         const int gl = g + t.n_it - 1;
         if (!mbar_wait(smem_u32(&bar->mm_done), gl & 1, abort_flag, p.err, kErrWaitSoftmax)) break;
         tc_fence_after();
-        __nv_bfloat16* drow = p.dqkv + qr * p.ld + t.head * HD + half * OH;
-#pragma unroll
-        for (int cc = 0; cc < OH / 32; ++cc) {
-          uint32_t dq[32];
-          CFB_TMEM_LD32(lane_addr + kColAcc + half * OH + cc * 32, dq);
-          tmem_ld_wait();
-          if (qvalid) store_row32(drow + cc * 32, dq, p.scale);
-        }
+        store_rot_pairs<HD>(lane_addr + kColAcc, p.dqkv + qr * p.ld + t.head * HD, half, p.scale,
+                            p.cs, qpos, qvalid);
       }
       // accumulators read: the next item's first accumulate may overwrite them
       tc_fence_before();
@@ -554,7 +596,7 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* ptr, long long rows, long lo
 int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, const void* do_k,
                     long long ld_o, const float* lse_k, const float* delta, const int* pos_k,
                     void* dqkv_k, int B, int S, int Sk, int nh, int nkv, int hd, float scale,
-                    int* work, int* err, cudaStream_t st) {
+                    const float* rope_cs, int* work, int* err, cudaStream_t st) {
   using namespace cfb;
   using namespace cfb::attn_bwd_tc;
   if (ld_qkv % 8 || ld_o % 8 || nh % nkv || Sk <= 0 || !work) return -11;
@@ -589,6 +631,7 @@ int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, c
   p.ld = ld_qkv;
   p.work = work;
   p.err = err;
+  p.cs = rope_cs;
   static int n_sm = 0;
   if (n_sm == 0) {
     int dev = 0;

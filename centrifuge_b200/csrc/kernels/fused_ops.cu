@@ -160,14 +160,103 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
   }
 }
 
-// out[c] += sum_p partial[p, c]
-__global__ void colsum_acc_kernel(const float* __restrict__ partial, float* __restrict__ out,
-                                  int P, int H) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= H) return;
+// Warp per row: the lane owns NG groups of 8 columns, c = (lane + 32 g) * 8, and keeps their
+// dgamma partial sums in registers across the rows of its warp.  Pass 1 reads dy, x for the row
+// dot product; pass 2 re-reads them (L1-resident) to write dx.  No block barrier per row.
+template <int NG>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+    const int* __restrict__ x_rows, const float* __restrict__ rstd,
+    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ dres,
+    __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_partial, int rows, int H) {
+  const int lane = lane_id(), wp = warp_id();
+  float dw[NG][8];
+#pragma unroll
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dw[g][i] = 0.f;
+  const float inv_h = 1.f / static_cast<float>(H);
+  for (int r = blockIdx.x * 8 + wp; r < rows; r += gridDim.x * 8) {
+    const long long xr = x_rows ? x_rows[r] : r;
+    const float rs = rstd[xr];
+    const __nv_bfloat16* dyr = dy + static_cast<long long>(r) * H;
+    const __nv_bfloat16* xrp = x + xr * H;
+    float dot = 0.f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const int c = (lane + 32 * g) * 8;
+      if (c < H) {
+        float a[8], b[8], wv[8];
+        load8(dyr + c, a);
+        load8(xrp + c, b);
+        load8(w + c, wv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float t = a[i] * b[i];
+          dot += wv[i] * t;
+          dw[g][i] += t * rs;
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float coef = dot * rs * rs * rs * inv_h;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const int c = (lane + 32 * g) * 8;
+      if (c < H) {
+        float a[8], b[8], wv[8], o[8];
+        load8(dyr + c, a);
+        load8(xrp + c, b);
+        load8(w + c, wv);
+        if (dres) {
+          load8(dres + static_cast<long long>(r) * H + c, o);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] += rs * wv[i] * a[i] - b[i] * coef;
+        store8(dx + static_cast<long long>(r) * H + c, o);
+      }
+    }
+  }
+  // block reduction of the eight warps' partial sums (256 columns at a time), then one partial
+  // row per block
+  __shared__ float red[8][256];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) red[wp][lane * 8 + i] = dw[g][i];
+    __syncthreads();
+    const int c = g * 256 + threadIdx.x;
+    if (c < H) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t += red[k][threadIdx.x];
+      dw_partial[static_cast<long long>(blockIdx.x) * H + c] = t;
+    }
+    __syncthreads();
+  }
+}
+
+// out[c] += sum_p partial[p, c].  Block = 32 columns x 8 row slices; the slices are combined
+// in a fixed order (deterministic).
+__global__ void __launch_bounds__(256) colsum_acc_kernel(const float* __restrict__ partial,
+                                                         float* __restrict__ out, int P, int H) {
+  __shared__ float red[8][33];
+  const int cx = threadIdx.x & 31, ry = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + cx;
   float s = 0.f;
-  for (int p = 0; p < P; ++p) s += partial[static_cast<long long>(p) * H + c];
-  out[c] += s;
+  if (c < H)
+    for (int p = ry; p < P; p += 8) s += partial[static_cast<long long>(p) * H + c];
+  red[ry][cx] = s;
+  __syncthreads();
+  if (ry == 0 && c < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][cx];
+    out[c] += t;
+  }
 }
 
 // ---------------------------------------------------------------- RoPE
@@ -633,13 +722,27 @@ int cfb_rmsnorm_bwd(const void* dy, const void* x, const int* x_rows, const floa
   const bf16* c = static_cast<const bf16*>(w);
   const bf16* d = static_cast<const bf16*>(dres);
   bf16* o = static_cast<bf16*>(dx);
-  switch (groups) {
-    case 1: rmsnorm_bwd_kernel<1><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
-    case 2: rmsnorm_bwd_kernel<2><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
-    case 3: rmsnorm_bwd_kernel<3><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
-    default: rmsnorm_bwd_kernel<4><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+  bool done = false;
+  if (H % 256 == 0) {  // warp-per-row kernel
+    done = true;
+    switch (H / 256) {
+      case 1: rmsnorm_bwd_warp_kernel<1><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      case 2: rmsnorm_bwd_warp_kernel<2><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      case 4: rmsnorm_bwd_warp_kernel<4><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      case 8: rmsnorm_bwd_warp_kernel<8><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      case 16: rmsnorm_bwd_warp_kernel<16><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      default: done = false;
+    }
   }
-  colsum_acc_kernel<<<(H + 255) / 256, 256, 0, st>>>(dw_partial, dw_acc, partial_rows, H);
+  if (!done) {
+    switch (groups) {
+      case 1: rmsnorm_bwd_kernel<1><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      case 2: rmsnorm_bwd_kernel<2><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      case 3: rmsnorm_bwd_kernel<3><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+      default: rmsnorm_bwd_kernel<4><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
+    }
+  }
+  colsum_acc_kernel<<<(H + 31) / 32, 256, 0, st>>>(dw_partial, dw_acc, partial_rows, H);
   return last_err();
 }
 

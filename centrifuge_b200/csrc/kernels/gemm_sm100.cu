@@ -32,6 +32,11 @@ struct GemmArgs {
   long long ldr;
   float alpha;
   int* err;
+  // kEpiBF16Rope: rotate-half RoPE of columns [0, rope_cols) in heads of hd columns, at
+  // position pos[row], with the table cs [max_pos, hd/2, 2] fp32 (cos, sin)
+  const int* pos;
+  const float* cs;
+  int rope_cols, hd;
 };
 
 template <int BN>
@@ -224,6 +229,40 @@ __global__ void __launch_bounds__(192, 1)
       for (int c = 0; c < BN / 32; ++c) {
         const int col = n0 + c * 32;
         if (col >= p.N) break;  // warp-uniform
+        if (EPI == kEpiBF16Rope && col < p.rope_cols) {
+          // the first-half chunk of a head rotates together with its partner hd/2 columns on
+          const int half = p.hd >> 1;
+          const int hc = col % p.hd;
+          if (hc >= half) continue;  // already written with its partner (warp-uniform)
+          uint32_t ra[32], rb[32];
+          CFB_TMEM_LD32(taddr + c * 32, ra);
+          CFB_TMEM_LD32(taddr + c * 32 + half, rb);
+          tmem_ld_wait();
+          if (row < p.M) {
+            const float4* cs =
+                reinterpret_cast<const float4*>(p.cs + (static_cast<long long>(p.pos[row]) * half + hc) * 2);
+            uint32_t oa[16], ob[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const float4 q = __ldg(cs + t);  // cos, sin of pairs 2t and 2t+1
+              const float a0 = __uint_as_float(ra[2 * t]) * p.alpha;
+              const float a1 = __uint_as_float(ra[2 * t + 1]) * p.alpha;
+              const float b0 = __uint_as_float(rb[2 * t]) * p.alpha;
+              const float b1 = __uint_as_float(rb[2 * t + 1]) * p.alpha;
+              oa[t] = pack_bf16x2(a0 * q.x - b0 * q.y, a1 * q.z - b1 * q.w);
+              ob[t] = pack_bf16x2(b0 * q.x + a0 * q.y, b1 * q.z + a1 * q.w);
+            }
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+            uint4* da = reinterpret_cast<uint4*>(dst);
+            uint4* db = reinterpret_cast<uint4*>(dst + half);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              da[j] = make_uint4(oa[4 * j], oa[4 * j + 1], oa[4 * j + 2], oa[4 * j + 3]);
+              db[j] = make_uint4(ob[4 * j], ob[4 * j + 1], ob[4 * j + 2], ob[4 * j + 3]);
+            }
+          }
+          continue;
+        }
         uint32_t r[32];
         CFB_TMEM_LD32(taddr + c * 32, r);
         tmem_ld_wait();
@@ -231,7 +270,7 @@ __global__ void __launch_bounds__(192, 1)
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
-          if (EPI == kEpiBF16 || EPI == kEpiBF16Resid) {
+          if (EPI == kEpiBF16 || EPI == kEpiBF16Resid || EPI == kEpiBF16Rope) {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
             if (EPI == kEpiBF16Resid) {
               const uint4* rs = reinterpret_cast<const uint4*>(p.R + row * p.ldr + col);
@@ -363,6 +402,9 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
       return dispatch_major<BN, kEpiBF16Resid>(a_mn, b_mn, ta, tb, a, st, max_ctas);
     case kEpiF32: return dispatch_major<BN, kEpiF32>(a_mn, b_mn, ta, tb, a, st, max_ctas);
     case kEpiF32Acc: return dispatch_major<BN, kEpiF32Acc>(a_mn, b_mn, ta, tb, a, st, max_ctas);
+    case kEpiBF16Rope:  // forward projections only: both operands K-major
+      if (a_mn || b_mn) return -4;
+      return launch_gemm<BN, false, false, kEpiBF16Rope>(ta, tb, a, st, max_ctas);
   }
   return -4;
 }
@@ -371,9 +413,10 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
 
 using namespace cfb;
 
-int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
-                  void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
-                  int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st) {
+static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, long long ldb,
+                      int b_mn, void* D, long long ldd, int epi, const void* R, long long ldr,
+                      int M, int N, int K, float alpha, int* err, int bn, int max_ctas,
+                      const int* pos, const float* cs, int rope_cols, int hd, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0) return -10;
   if ((N % 32) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -11;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
@@ -402,6 +445,29 @@ int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long lo
   a.ldr = ldr;
   a.alpha = alpha;
   a.err = err;
+  a.pos = pos;
+  a.cs = cs;
+  a.rope_cols = rope_cols;
+  a.hd = hd;
   if (bn == 256) return dispatch_epi<256>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
   return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
+}
+
+int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
+                  void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
+                  int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st) {
+  if (epi == kEpiBF16Rope) return -4;
+  return gemm_entry(A, lda, a_mn, B, ldb, b_mn, D, ldd, epi, R, ldr, M, N, K, alpha, err, bn,
+                    max_ctas, nullptr, nullptr, 0, 0, st);
+}
+
+int cfb_gemm_bf16_rope(const void* A, long long lda, const void* B, long long ldb, void* D,
+                       long long ldd, int M, int N, int K, const int* pos, const float* cos_sin,
+                       int rope_cols, int head_dim, int* err, int bn, int max_ctas,
+                       cudaStream_t st) {
+  if (head_dim != 64 && head_dim != 128) return -13;
+  if (rope_cols < 0 || rope_cols % head_dim || rope_cols > N || !pos || !cos_sin) return -13;
+  if (reinterpret_cast<uintptr_t>(cos_sin) & 15) return -12;
+  return gemm_entry(A, lda, 0, B, ldb, 0, D, ldd, kEpiBF16Rope, nullptr, 0, M, N, K, 1.0f, err,
+                    bn, max_ctas, pos, cos_sin, rope_cols, head_dim, st);
 }

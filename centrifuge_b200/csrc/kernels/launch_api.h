@@ -6,12 +6,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3 };
+enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3, kEpiBF16Rope = 4 };
 
 // GEMM (gemm_sm100.cu): D = alpha * op(A) op(B) with the epilogue `epi`.
 int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
                   int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st);
+// Forward projection with rotate-half RoPE fused into the epilogue: D = A B^T (both K-major) and
+// columns [0, rope_cols) rotated per head of head_dim (64 or 128) at position pos[row], using the
+// [max_pos, head_dim/2, 2] fp32 (cos, sin) table.
+int cfb_gemm_bf16_rope(const void* A, long long lda, const void* B, long long ldb, void* D,
+                       long long ldd, int M, int N, int K, const int* pos, const float* cos_sin,
+                       int rope_cols, int head_dim, int* err, int bn, int max_ctas,
+                       cudaStream_t st);
 
 // Row ops (fused_ops.cu).
 int cfb_rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int rows, int H,
@@ -70,13 +77,14 @@ int cfb_attn_bwd(const void* qkv_k, long long ld_qkv, const void* qkv_full, cons
 int cfb_attn_delta(const void* o_k, const void* do_k, long long ld_o, float* delta, long long rows,
                    int nh, int hd, cudaStream_t st);
 // tcgen05/TMEM filtered backward (attention_bwd_sm100.cu): dK/dV of the kept keys and dQ of the
-// kept queries over all keys by position; `delta` must be computed first.  Persistent kernel
+// kept queries over all keys by position; `delta` must be computed first.  `rope_cs` (optional,
+// [max_pos, hd/2, 2] fp32 cos/sin) folds the RoPE backward of dQ and dK into the epilogue.  Persistent kernel
 // scheduled through `work` (two device int32 words, zero before the first launch; the kernel
 // leaves them zero).  Launches sharing one `work` pair must be ordered (one stream).
 int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, const void* do_k,
                     long long ld_o, const float* lse_k, const float* delta, const int* pos_k,
                     void* dqkv_k, int B, int S, int Sk, int nh, int nkv, int hd, float scale,
-                    int* work, int* err, cudaStream_t st);
+                    const float* rope_cs, int* work, int* err, cudaStream_t st);
 
 // NVLink peer-memory gradient reduction (comm_sm100.cu).
 int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,

@@ -165,8 +165,8 @@ class LlamaCore(torch.nn.Module):
             pre = f"layers.{i}."
             L = {"x": x}
             xn, rstd1 = fused.rmsnorm_fwd(x, p[pre + "ln1"], cfg.rms_norm_eps)
-            qkv = G.linear_fwd(xn, p[pre + "wqkv"])
-            fused.rope_(qkv, pos, nh + nkv, hd, self._rope)
+            # RoPE of the q and k heads runs in the projection's epilogue
+            qkv = G.linear_fwd_rope(xn, p[pre + "wqkv"], pos, self._rope, (nh + nkv) * hd, hd)
             o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd, scale=self.scale)
             x2 = G.linear_fwd(o, p[pre + "wo"], resid=x)
             xn2, rstd2 = fused.rmsnorm_fwd(x2, p[pre + "ln2"], cfg.rms_norm_eps)
@@ -262,9 +262,9 @@ class LlamaCore(torch.nn.Module):
             lse_k = self._gather(L["lse"], rows)
             dqkv = fused.attn_bwd(qkv_k, L["qkv"], o_k, do, lse_k,
                                   pos2d if pos2d is not None else pos_flat.view(B, S),
-                                  B, S, Sk, nh, nkv, hd, scale=self.scale)
+                                  B, S, Sk, nh, nkv, hd, scale=self.scale,
+                                  rope_table=self._rope)  # RoPE backward in the epilogue
             del qkv_k, lse_k, o_k, do
-            fused.rope_(dqkv, pos_flat, nh + nkv, hd, self._rope, inverse=True)
             xn_k = self._gather(L["xn"], rows)
             G.linear_wgrad(dqkv, xn_k, g[pre + "wqkv"])
             dxn = G.linear_dgrad(dqkv, p[pre + "wqkv"])

@@ -157,8 +157,8 @@ class TPLlamaCore(torch.nn.Module):
             L = {"x": x}
             xn_p, r1 = fused.rmsnorm_fwd(x, p[pre + "ln1"], cfg.rms_norm_eps)
             xn = tp.all_gather_rows(xn_p)
-            qkv = G.linear_fwd(xn, p[pre + "wqkv"])
-            fused.rope_(qkv, pos, nh + nkv, hd, self._rope)
+            # RoPE of the q and k heads runs in the projection's epilogue
+            qkv = G.linear_fwd_rope(xn, p[pre + "wqkv"], pos, self._rope, (nh + nkv) * hd, hd)
             o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd, scale=self.scale)
             part = G.linear_fwd(o, p[pre + "wo"])
             x2 = tp.reduce_scatter_rows(part) + x if P > 1 else G.linear_fwd(o, p[pre + "wo"], resid=x)
@@ -261,9 +261,9 @@ class TPLlamaCore(torch.nn.Module):
             lse_k = L["lse"] if rows is None else _gather(L["lse"], rows)
             dqkv = fused.attn_bwd(qkv_k, L["qkv"], o_k, do, lse_k,
                                   pos2d if pos2d is not None else pos_flat.view(B, S),
-                                  B, S, Sk, nh, nkv, hd, scale=self.scale)
+                                  B, S, Sk, nh, nkv, hd, scale=self.scale,
+                                  rope_table=self._rope)  # RoPE backward in the epilogue
             del qkv_k, lse_k, o_k, do
-            fused.rope_(dqkv, pos_flat, nh + nkv, hd, self._rope, inverse=True)
             xn_k = gat(L["xn"])
             G.linear_wgrad(dqkv, xn_k, g[pre + "wqkv"])
             dxn_p = rs(G.linear_dgrad(dqkv, p[pre + "wqkv"]))

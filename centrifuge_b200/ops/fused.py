@@ -255,8 +255,12 @@ def attn_fwd(qkv: torch.Tensor, B: int, S: int, nh: int, nkv: int, hd: int,
 def attn_bwd(qkv_k: torch.Tensor, qkv_full: torch.Tensor, o_k: torch.Tensor, do_k: torch.Tensor,
              lse_k: torch.Tensor, pos_k: torch.Tensor, B: int, S: int, Sk: int, nh: int,
              nkv: int, hd: int, dqkv_k: Optional[torch.Tensor] = None,
-             scale: Optional[float] = None) -> torch.Tensor:
-    """Filtered (restore-Q) attention backward; returns ``dqkv_k [B*Sk, ld]``."""
+             scale: Optional[float] = None,
+             rope_table: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Filtered (restore-Q) attention backward; returns ``dqkv_k [B*Sk, ld]``.
+
+    With ``rope_table`` the q and k gradients come out with the RoPE backward applied (rotated
+    back to the pre-RoPE projection outputs at the kept rows' positions)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(hd)
     if dqkv_k is None:
         dqkv_k = torch.empty_like(qkv_k)
@@ -267,10 +271,20 @@ def attn_bwd(qkv_k: torch.Tensor, qkv_full: torch.Tensor, o_k: torch.Tensor, do_
         dq, dk, dv = ref.attention_bwd_filtered(
             q, k, v, o_k.reshape(B, Sk, nh, hd), do_k.reshape(B, Sk, nh, hd),
             lse_k.reshape(B, Sk, nh), pos_k.reshape(B, Sk), scale)
+        dq = dq.reshape(B * Sk, nh, hd)
+        dk = dk.reshape(B * Sk, nkv, hd)
+        if rope_table is not None:
+            pf = pos_k.reshape(-1)
+            dq = ref.rope(dq, pf, rope_table, inverse=True)
+            dk = ref.rope(dk, pf, rope_table, inverse=True)
         dqkv_k[:, : nh * hd] = dq.reshape(B * Sk, nh * hd)
         dqkv_k[:, nh * hd:(nh + nkv) * hd] = dk.reshape(B * Sk, nkv * hd)
         dqkv_k[:, (nh + nkv) * hd:(nh + 2 * nkv) * hd] = dv.reshape(B * Sk, nkv * hd)
         return dqkv_k
+    delta = torch.empty(B * Sk * nh, dtype=torch.float32, device=qkv_k.device)
+    kernels().attn_bwd(qkv_k, qkv_full, o_k, do_k, lse_k, pos_k, dqkv_k, delta, B, S, Sk, nh, nkv,
+                       hd, scale, rope_table)
+    return dqkv_k
     delta = torch.empty(B * Sk * nh, dtype=torch.float32, device=qkv_k.device)
     kernels().attn_bwd(qkv_k, qkv_full, o_k, do_k, lse_k, pos_k, dqkv_k, delta, B, S, Sk, nh, nkv,
                        hd, scale)

@@ -46,6 +46,26 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = N
                 resid)
 
 
+def linear_fwd_rope(x: torch.Tensor, w: torch.Tensor, pos: torch.Tensor, table: torch.Tensor,
+                    rope_cols: int, head_dim: int, out: Optional[torch.Tensor] = None
+                    ) -> torch.Tensor:
+    """``y = x w^T`` with rotate-half RoPE applied to columns ``[0, rope_cols)`` (heads of
+    ``head_dim``) at positions ``pos [T]``, fused into the GEMM epilogue (the q and k heads of a
+    fused qkv projection)."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    if not x.is_cuda:
+        from . import reference as ref
+        y = x.float() @ w.float().t()
+        n = rope_cols // head_dim
+        q = y[:, :rope_cols].view(-1, n, head_dim)
+        y[:, :rope_cols] = ref.rope(q, pos, table).reshape(-1, rope_cols)
+        out.copy_(y)
+        return out
+    kernels().gemm_rope(x, w, out, pos, table, rope_cols, head_dim)
+    return out
+
+
 def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
                  resid: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:

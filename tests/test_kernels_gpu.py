@@ -52,17 +52,18 @@ def test_gemm_epilogues():
     assert rel_err(dw, 0.5 * dy.float().t() @ x.float()) < 1e-2
 
 
-def test_rmsnorm():
+@pytest.mark.parametrize("T,H,Tk", [(300, 2048, 100), (9000, 2048, 4500), (3000, 4096, 1200),
+                                   (500, 1000, 250), (700, 768, 700)])
+def test_rmsnorm(T, H, Tk):
     torch.manual_seed(2)
-    T, H = 300, 2048
     x = torch.randn(T, H, device=dev).bfloat16()
     w = (1 + 0.1 * torch.randn(H, device=dev)).bfloat16()
     y, rstd = fused.rmsnorm_fwd(x, w, 1e-5)
     yr, rr = ref.rmsnorm(x, w, 1e-5)
     assert rel_err(y, yr) < 1e-2 and rel_err(rstd, rr) < 1e-4
-    rows = torch.randperm(T, device=dev)[:100].sort().values.int()
-    dy = torch.randn(100, H, device=dev).bfloat16()
-    dres = torch.randn(100, H, device=dev).bfloat16()
+    rows = torch.randperm(T, device=dev)[:Tk].sort().values.int()
+    dy = torch.randn(Tk, H, device=dev).bfloat16()
+    dres = torch.randn(Tk, H, device=dev).bfloat16()
     dw = torch.zeros(H, device=dev)
     dx = fused.rmsnorm_bwd(dy, x, rstd, w, dw, x_rows=rows, dres=dres)
     dxr, dwr = ref.rmsnorm_bwd(dy, x[rows.long()], rstd[rows.long()], w, dres)
@@ -196,6 +197,55 @@ def test_attention_fwd(B, S, nh, nkv, hd):
     o2, l2 = torch.empty_like(o), torch.empty_like(lse)
     kernels().attn_fwd_mma(qkv, o2, l2, B, S, nh, nkv, hd, 1.0 / hd ** 0.5)
     assert rel_err(o2, o) < 1e-2 and rel_err(l2, lse) < 1e-4
+
+
+@pytest.mark.parametrize("M,nh,nkv,hd,bn", [(4096, 32, 4, 64, 0), (1000, 8, 2, 128, 128),
+                                            (333, 4, 4, 64, 256), (2048, 16, 8, 128, 256)])
+def test_gemm_rope_epilogue(M, nh, nkv, hd, bn):
+    """QKV projection with RoPE in the epilogue vs the fp32 projection followed by RoPE."""
+    from centrifuge_b200.ops import kernels
+    torch.manual_seed(12)
+    K = 512
+    N = (nh + 2 * nkv) * hd
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(N, K, device=dev) / K ** 0.5).bfloat16()
+    table = ref.rope_table(4096, hd, 10000.0, dev)
+    pos = torch.randint(0, 4096, (M,), device=dev, dtype=torch.int32)
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    kernels().gemm_rope(x, w, out, pos, table, (nh + nkv) * hd, hd, bn)
+    y = x.float() @ w.float().t()
+    rc = (nh + nkv) * hd
+    y[:, :rc] = ref.rope(y[:, :rc].view(M, nh + nkv, hd), pos, table).reshape(M, rc)
+    assert rel_err(out, y) < 1e-2
+    assert (out.float() - y).abs().max().item() < 0.05
+    assert kernels().gemm_error_word(0, True) == 0
+
+
+@pytest.mark.parametrize("B,S,nh,nkv,hd", [(2, 512, 8, 2, 64), (1, 700, 4, 1, 128)])
+def test_attention_bwd_rope_epilogue(B, S, nh, nkv, hd):
+    """The RoPE backward folded into the attention backward epilogue equals a separate inverse
+    rotation of the dq/dk blocks."""
+    torch.manual_seed(13)
+    ld = (nh + 2 * nkv) * hd
+    qkv = (0.5 * torch.randn(B * S, ld, device=dev)).bfloat16()
+    o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
+    Sk = S // 2
+    pos = torch.stack([torch.cat([torch.randperm(S - 1, device=dev)[: Sk - 1].sort().values,
+                                  torch.tensor([S - 1], device=dev)]) for _ in range(B)])
+    pos = pos.sort(dim=1).values.int()
+    flat = (pos + torch.arange(B, device=dev, dtype=torch.int32).view(B, 1) * S).reshape(-1)
+    qkv_k, o_k, lse_k = qkv[flat.long()].contiguous(), o[flat.long()].contiguous(), lse[flat.long()].contiguous()
+    do_k = torch.randn(B * Sk, nh * hd, device=dev).bfloat16()
+    table = ref.rope_table(4096, hd, 500000.0, dev)
+    d0 = fused.attn_bwd(qkv_k, qkv, o_k, do_k, lse_k, pos, B, S, Sk, nh, nkv, hd)
+    d1 = fused.attn_bwd(qkv_k, qkv, o_k, do_k, lse_k, pos, B, S, Sk, nh, nkv, hd,
+                        rope_table=table)
+    want = d0.float().clone()
+    rc = (nh + nkv) * hd
+    want[:, :rc] = ref.rope(want[:, :rc].view(-1, nh + nkv, hd), pos.reshape(-1), table,
+                            inverse=True).reshape(-1, rc)
+    assert rel_err(d1, want) < 1e-2
+    assert torch.equal(d1[:, rc:], d0[:, rc:])
 
 
 @pytest.mark.parametrize("B,S,nh,nkv,hd,amp", [(8, 2048, 32, 4, 64, 1.0), (4, 2048, 32, 8, 128, 1.0),
