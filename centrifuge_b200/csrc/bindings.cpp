@@ -120,6 +120,89 @@ void gemm_rope(const Tensor& a, const Tensor& b, Tensor& out, const Tensor& pos,
                "gemm_rope");
 }
 
+// ---- tensor-parallel fusions (pointers into symmetric memory are raw device addresses)
+void tp_rmsnorm_push(const Tensor& x, const Tensor& w, double eps, int64_t mc_dst,
+                     int64_t peer_dst_dev, int64_t ld_dst, Tensor& rstd, int64_t peer_flags_dev,
+                     int64_t flag_off, int64_t rank, int64_t P, int64_t shard_rows,
+                     int64_t epoch, Tensor& cnt) {
+  check_bf16_2d(x, "x");
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && w.numel() == x.size(1), "x, w");
+  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() >= x.size(0), "rstd");
+  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.is_cuda(), "cnt int32");
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_tp_rmsnorm_push(x.data_ptr(), w.data_ptr(), static_cast<int>(x.size(0)),
+                                   static_cast<int>(x.size(1)), static_cast<float>(eps),
+                                   reinterpret_cast<void*>(mc_dst),
+                                   reinterpret_cast<void* const*>(peer_dst_dev), ld_dst,
+                                   rstd.data_ptr<float>(),
+                                   reinterpret_cast<uint32_t* const*>(peer_flags_dev),
+                                   static_cast<int>(flag_off), static_cast<int>(rank),
+                                   static_cast<int>(P), static_cast<int>(shard_rows),
+                                   static_cast<uint32_t>(epoch),
+                                   reinterpret_cast<uint32_t*>(cnt.data_ptr<int>()),
+                                   cur_stream()),
+               "tp_rmsnorm_push");
+}
+
+// out = a @ b^T fused with a tensor-parallel collective (mode 1: all-gather consumer of `a`;
+// mode 2: reduce-scatter producer, `out` is this rank's partial buffer and `rs_out` receives
+// the reduced own rows plus `resid`).  Optional RoPE epilogue (mode 1) with pos/table.
+void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, const c10::optional<Tensor>& pos,
+             const c10::optional<Tensor>& table, int64_t rope_cols, int64_t hd, int64_t mode,
+             int64_t rank, int64_t P, int64_t shard_rows, int64_t epoch, int64_t a_ready,
+             int64_t peer_flags_dev, int64_t flag_ready, int64_t flag_done,
+             const c10::optional<Tensor>& tile_cnt, int64_t mc_part, int64_t peer_part_dev,
+             const c10::optional<Tensor>& resid, const c10::optional<Tensor>& rs_out,
+             int64_t bn) {
+  check_bf16_2d(a, "a");
+  check_bf16_2d(b, "b");
+  check_bf16_2d(out, "out");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K && out.size(0) == M && out.size(1) == N, "gemm_tp: shapes");
+  CfbTpGemm t = {};
+  t.mode = static_cast<int>(mode);
+  t.rank = static_cast<int>(rank);
+  t.P = static_cast<int>(P);
+  t.shard_rows = static_cast<int>(shard_rows);
+  t.epoch = static_cast<uint32_t>(epoch);
+  t.a_ready = reinterpret_cast<const uint32_t*>(a_ready);
+  t.peer_flags = reinterpret_cast<uint32_t* const*>(peer_flags_dev);
+  t.flag_ready = static_cast<int>(flag_ready);
+  t.flag_done = static_cast<int>(flag_done);
+  if (tile_cnt.has_value() && tile_cnt->defined()) {
+    TORCH_CHECK(tile_cnt->scalar_type() == at::kInt && tile_cnt->numel() >= P + 2, "tile_cnt");
+    t.tile_cnt = reinterpret_cast<uint32_t*>(tile_cnt->data_ptr<int>());
+  }
+  t.mc_part = reinterpret_cast<const void*>(mc_part);
+  t.peer_part = reinterpret_cast<const void* const*>(peer_part_dev);
+  if (resid.has_value() && resid->defined()) {
+    check_bf16_2d(*resid, "resid");
+    t.resid = resid->data_ptr();
+    t.ld_resid = resid->stride(0);
+  }
+  if (rs_out.has_value() && rs_out->defined()) {
+    check_bf16_2d(*rs_out, "rs_out");
+    TORCH_CHECK(rs_out->size(1) == N, "rs_out columns");
+    t.out = rs_out->data_ptr();
+    t.ld_out = rs_out->stride(0);
+  }
+  const int* pp = nullptr;
+  const float* cs = nullptr;
+  if (table.has_value() && table->defined()) {
+    TORCH_CHECK(pos.has_value() && pos->scalar_type() == at::kInt && pos->numel() == M, "pos");
+    TORCH_CHECK(table->scalar_type() == at::kFloat && table->is_contiguous(), "table");
+    pp = pos->data_ptr<int>();
+    cs = table->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard guard(a.device());
+  CFB_CHECK_RC(cfb_gemm_tp(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(),
+                           out.stride(0), static_cast<int>(M), static_cast<int>(N),
+                           static_cast<int>(K), pp, cs, static_cast<int>(rope_cols),
+                           static_cast<int>(hd), &t, err_word(a.get_device()).data_ptr<int>(),
+                           static_cast<int>(bn), cur_stream()),
+               "gemm_tp");
+}
+
 int64_t gemm_error_word(int64_t device, bool reset) {
   Tensor& w = err_word(static_cast<int>(device));
   const int64_t v = w.item<int>();
@@ -512,6 +595,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("resid") = py::none(),
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
+  m.def("tp_rmsnorm_push", &tp_rmsnorm_push);
+  m.def("gemm_tp", &gemm_tp, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("pos"),
+        py::arg("table"), py::arg("rope_cols"), py::arg("hd"), py::arg("mode"), py::arg("rank"),
+        py::arg("P"), py::arg("shard_rows"), py::arg("epoch"), py::arg("a_ready"),
+        py::arg("peer_flags_dev"), py::arg("flag_ready"), py::arg("flag_done"),
+        py::arg("tile_cnt"), py::arg("mc_part"), py::arg("peer_part_dev"), py::arg("resid"),
+        py::arg("rs_out"), py::arg("bn") = 0);
   m.def("gemm_rope", &gemm_rope, "tcgen05 bf16 GEMM with RoPE fused into the epilogue",
         py::arg("a"), py::arg("b"), py::arg("out"), py::arg("pos"), py::arg("table"),
         py::arg("rope_cols"), py::arg("hd"), py::arg("bn") = 0);

@@ -37,7 +37,66 @@ struct GemmArgs {
   const int* pos;
   const float* cs;
   int rope_cols, hd;
+  // ---- tensor-parallel fusion (sequence-parallel row shards of shard_mblocks 128-row blocks)
+  int rank, P, shard_mblocks;
+  uint32_t epoch;
+  // all-gather consumer (TPM 1): A rows of shard s are usable once a_ready[s] >= epoch (local
+  // flags raised by the producer of each shard); m-blocks are rotated by rot_mblocks so the
+  // rank's own shard, ready first, is computed first
+  const uint32_t* a_ready;
+  int rot_mblocks;
+  // reduce-scatter producer (TPM 2): D is this rank's partial-sum buffer (symmetric memory);
+  // flags live in symmetric buffers peer_flags[q] (rs_ready at flag_ready, rs_done at
+  // flag_done, P entries each); tile_cnt is local scratch [P + 2], zero at rest
+  uint32_t* const* peer_flags;
+  int flag_ready, flag_done;
+  uint32_t* tile_cnt;
+  const __nv_bfloat16* mc_part;            // multicast address of D, or nullptr
+  const __nv_bfloat16* const* peer_part;   // D of every rank (peer loads when no multicast)
+  const __nv_bfloat16* rs_resid;           // [shard rows, N] added to the reduced rows
+  __nv_bfloat16* rs_out;                   // [shard rows, N] reduced rows of this rank
+  long long ld_resid, ld_out;
 };
+
+namespace tpc {
+constexpr uint64_t kPeerWaitNs = 20000000000ull;  // 20 s
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* f) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* f, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+// Bounded wait until (int)(flags[i] - epoch) >= 0 for i < n.  On timeout raises *abort and
+// records kErrPeerWait; returns false.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* flags, int n, uint32_t epoch,
+                                           volatile int* abort, int* err) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int i = 0; i < n; ++i) {
+    uint32_t spins = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(flags + i) - epoch) < 0) {
+      if ((++spins & 255u) == 0) {
+        if (*abort) return false;
+        if (globaltimer_ns() - t0 > kPeerWaitNs) {
+          *abort = 1;
+          atomicCAS(err, 0, kErrPeerWait);
+          return false;
+        }
+      }
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ uint4 ld_reduce_bf16x8(const __nv_bfloat16* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
+}  // namespace tpc
 
 template <int BN>
 struct GemmShape {
@@ -62,8 +121,10 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   tn = r / gsize;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+// TPM: 0 plain; 1 all-gather consumer (A shards waited on per m-block); 2 reduce-scatter
+// producer (partials + per-shard signals + two pull warps that reduce this rank's rows)
+template <int BN, bool A_MN, bool B_MN, int EPI, int TPM = 0>
+__global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
   using S = GemmShape<BN>;
@@ -121,9 +182,23 @@ __global__ void __launch_bounds__(192, 1)
       int last_stage = -1;
       uint32_t last_phase = 0;
       bool ok = true;
+      uint64_t ready_mask = 0;  // TPM 1: shards known to be gathered
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int tm, tn;
         tile_coords(tile, num_m, num_n, tm, tn);
+        if (TPM == 1) {
+          tm = (tm + p.rot_mblocks) % num_m;
+          const int sh = tm / p.shard_mblocks;
+          if (!((ready_mask >> sh) & 1ull)) {
+            if (!tpc::wait_epoch(p.a_ready + sh, 1, p.epoch, abort_flag, p.err)) {
+              ok = false;
+              break;
+            }
+            // rows written by peers' generic stores are read below by the TMA (async proxy)
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            ready_mask |= 1ull << sh;
+          }
+        }
         const int m0 = tm * S::BM, n0 = tn * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err,
@@ -209,14 +284,24 @@ __global__ void __launch_bounds__(192, 1)
       volatile int dummy = 0;
       mbar_wait(smem_u32(drain), 0, &dummy, nullptr, 0);
     }
-  } else {
+  } else if (warp < 6) {
     // -------------------------------------------------------------- epilogue (warps 2..5)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
     int it = 0;
+    if (TPM == 2) {
+      // the partial buffer of this epoch was last read by the pulls of epoch - 2
+      bool okw = true;
+      if (lane == 0)
+        okw = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_done, p.P, p.epoch - 2, abort_flag,
+                              p.err);
+      (void)__shfl_sync(0xffffffffu, okw ? 1 : 0, 0);  // on timeout abort_flag is raised
+    }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      if (TPM == 2 && *abort_flag) break;
       int tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
+      if (TPM == 1) tm = (tm + p.rot_mblocks) % num_m;
       const int m0 = tm * S::BM, n0 = tn * BN;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
@@ -317,6 +402,89 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
+      if (TPM == 2 && lane == 0) {
+        // count this warp's quarter of the tile; the last of a shard's tiles tells its owner
+        const int sh = tm / p.shard_mblocks;
+        const int sh_tiles = min(p.shard_mblocks, num_m - sh * p.shard_mblocks) * num_n;
+        __threadfence_system();
+        if (atomicAdd(p.tile_cnt + sh, 1u) == static_cast<uint32_t>(4 * sh_tiles - 1)) {
+          __threadfence_system();
+          tpc::st_release_sys(p.peer_flags[sh] + p.flag_ready + p.rank, p.epoch);
+        }
+      }
+    }
+  } else if (TPM == 2) {
+    // -------------------------------------------------------------- pull warps (6, 7)
+    // Rows [rank * shard, (rank + 1) * shard) summed over all ranks' partial buffers (one
+    // multimem.ld_reduce per 8 bf16 through the NVSwitch, fp32 accumulation), plus the
+    // residual, written to rs_out.  Starts as soon as every rank has finished this shard.
+    bool ok = true;
+    if (lane == 0)
+      ok = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_ready, p.P, p.epoch, abort_flag, p.err);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (ok) {
+      const int shard_rows = p.shard_mblocks * S::BM;
+      const int r_lo = p.rank * shard_rows;
+      const int rows = max(0, min(p.M - r_lo, shard_rows));
+      const int vec_per_row = p.N / 8;
+      const long long total = static_cast<long long>(rows) * vec_per_row;
+      const int t = (warp - 6) * 32 + lane;
+      for (long long v = static_cast<long long>(blockIdx.x) * 64 + t; v < total;
+           v += static_cast<long long>(gridDim.x) * 64) {
+        const int r = static_cast<int>(v / vec_per_row);
+        const int c = static_cast<int>(v % vec_per_row) * 8;
+        const long long off = static_cast<long long>(r_lo + r) * p.ldd + c;
+        float acc[8];
+        if (p.mc_part) {
+          const uint4 u = tpc::ld_reduce_bf16x8(p.mc_part + off);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            acc[2 * e] = f.x;
+            acc[2 * e + 1] = f.y;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+          for (int q2 = 0; q2 < p.P; ++q2) {
+            const uint4 u = *reinterpret_cast<const uint4*>(p.peer_part[q2] + off);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(h[e]);
+              acc[2 * e] += f.x;
+              acc[2 * e + 1] += f.y;
+            }
+          }
+        }
+        if (p.rs_resid) {
+          const uint4 u = *reinterpret_cast<const uint4*>(p.rs_resid + static_cast<long long>(r) * p.ld_resid + c);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            acc[2 * e] += f.x;
+            acc[2 * e + 1] += f.y;
+          }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c) = o;
+      }
+      // this rank has read its rows of every partial buffer: the last pull warp of the grid
+      // tells all ranks (their buffer of this epoch may be rewritten at epoch + 2)
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_system();
+        if (atomicAdd(p.tile_cnt + p.P, 1u) == 2u * gridDim.x - 1u) {
+          for (int q2 = 0; q2 < p.P; ++q2)
+            tpc::st_release_sys(p.peer_flags[q2] + p.flag_done + p.rank, p.epoch);
+        }
+      }
     }
   }
 
@@ -324,6 +492,13 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, S::TMEM_COLS);
+  if (TPM == 2 && threadIdx.x == 0) {
+    // the last CTA to finish clears the local counters for the next launch
+    __threadfence();
+    if (atomicAdd(p.tile_cnt + p.P + 1, 1u) == gridDim.x - 1u) {
+      for (int i = 0; i <= p.P + 1; ++i) atomicExch(p.tile_cnt + i, 0u);
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -367,11 +542,11 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, int TPM = 0>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                        cudaStream_t st, int max_ctas) {
   using S = GemmShape<BN>;
-  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI, TPM>;
   static bool configured = false;
   if (!configured) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
@@ -380,6 +555,22 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   const int tiles = ((a.M + 127) / 128) * ((a.N + BN - 1) / BN);
   int grid = tiles < num_sms() ? tiles : num_sms();
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+  if (TPM == 2) {
+    // CTAs wait on one another's tiles (through the shard flags): cooperative launch makes
+    // the whole grid co-resident
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = S::SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
+    return e == cudaSuccess ? 0 : -3;
+  }
   kern<<<grid, 192, S::SMEM_BYTES, st>>>(ta, tb, a);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
@@ -416,7 +607,8 @@ using namespace cfb;
 static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, long long ldb,
                       int b_mn, void* D, long long ldd, int epi, const void* R, long long ldr,
                       int M, int N, int K, float alpha, int* err, int bn, int max_ctas,
-                      const int* pos, const float* cs, int rope_cols, int hd, cudaStream_t st) {
+                      const int* pos, const float* cs, int rope_cols, int hd,
+                      const CfbTpGemm* tp, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0) return -10;
   if ((N % 32) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -11;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
@@ -449,6 +641,59 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.cs = cs;
   a.rope_cols = rope_cols;
   a.hd = hd;
+  a.rank = 0;
+  a.P = 1;
+  a.shard_mblocks = 1;
+  a.epoch = 0;
+  a.a_ready = nullptr;
+  a.rot_mblocks = 0;
+  a.peer_flags = nullptr;
+  a.flag_ready = a.flag_done = 0;
+  a.tile_cnt = nullptr;
+  a.mc_part = nullptr;
+  a.peer_part = nullptr;
+  a.rs_resid = nullptr;
+  a.rs_out = nullptr;
+  a.ld_resid = a.ld_out = 0;
+  if (tp) {
+    if (tp->mode != 1 && tp->mode != 2) return -13;
+    if (a_mn || b_mn) return -13;  // forward / dgrad-as-forward layouts only
+    if (tp->shard_rows % 128 || tp->P < 1 || tp->P > 64 || M > tp->P * tp->shard_rows)
+      return -13;
+    a.rank = tp->rank;
+    a.P = tp->P;
+    a.shard_mblocks = tp->shard_rows / 128;
+    a.epoch = tp->epoch;
+    if (tp->mode == 1) {
+      if (!tp->a_ready) return -13;
+      a.a_ready = tp->a_ready;
+      a.rot_mblocks = tp->rank * a.shard_mblocks;
+      if (epi == kEpiBF16) {
+        return bn == 256 ? launch_gemm<256, false, false, kEpiBF16, 1>(ta, tb, a, st, max_ctas)
+                         : launch_gemm<128, false, false, kEpiBF16, 1>(ta, tb, a, st, max_ctas);
+      }
+      if (epi == kEpiBF16Rope) {
+        return bn == 256 ? launch_gemm<256, false, false, kEpiBF16Rope, 1>(ta, tb, a, st, max_ctas)
+                         : launch_gemm<128, false, false, kEpiBF16Rope, 1>(ta, tb, a, st, max_ctas);
+      }
+      return -4;
+    }
+    if (epi != kEpiBF16 || !tp->peer_flags || !tp->tile_cnt || !tp->out ||
+        (!tp->mc_part && !tp->peer_part) || (N % 8))
+      return -13;
+    a.peer_flags = tp->peer_flags;
+    a.flag_ready = tp->flag_ready;
+    a.flag_done = tp->flag_done;
+    a.tile_cnt = tp->tile_cnt;
+    a.mc_part = static_cast<const __nv_bfloat16*>(tp->mc_part);
+    a.peer_part = reinterpret_cast<const __nv_bfloat16* const*>(tp->peer_part);
+    a.rs_resid = static_cast<const __nv_bfloat16*>(tp->resid);
+    a.rs_out = static_cast<__nv_bfloat16*>(tp->out);
+    a.ld_resid = tp->ld_resid;
+    a.ld_out = tp->ld_out;
+    return bn == 256 ? launch_gemm<256, false, false, kEpiBF16, 2>(ta, tb, a, st, max_ctas)
+                     : launch_gemm<128, false, false, kEpiBF16, 2>(ta, tb, a, st, max_ctas);
+  }
   if (bn == 256) return dispatch_epi<256>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
   return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
 }
@@ -458,7 +703,7 @@ int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long lo
                   int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st) {
   if (epi == kEpiBF16Rope) return -4;
   return gemm_entry(A, lda, a_mn, B, ldb, b_mn, D, ldd, epi, R, ldr, M, N, K, alpha, err, bn,
-                    max_ctas, nullptr, nullptr, 0, 0, st);
+                    max_ctas, nullptr, nullptr, 0, 0, nullptr, st);
 }
 
 int cfb_gemm_bf16_rope(const void* A, long long lda, const void* B, long long ldb, void* D,
@@ -469,5 +714,16 @@ int cfb_gemm_bf16_rope(const void* A, long long lda, const void* B, long long ld
   if (rope_cols < 0 || rope_cols % head_dim || rope_cols > N || !pos || !cos_sin) return -13;
   if (reinterpret_cast<uintptr_t>(cos_sin) & 15) return -12;
   return gemm_entry(A, lda, 0, B, ldb, 0, D, ldd, kEpiBF16Rope, nullptr, 0, M, N, K, 1.0f, err,
-                    bn, max_ctas, pos, cos_sin, rope_cols, head_dim, st);
+                    bn, max_ctas, pos, cos_sin, rope_cols, head_dim, nullptr, st);
+}
+
+int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, void* D,
+                long long ldd, int M, int N, int K, const int* pos, const float* cos_sin,
+                int rope_cols, int head_dim, const CfbTpGemm* tp, int* err, int bn,
+                cudaStream_t st) {
+  if (!tp) return -13;
+  const int epi = cos_sin ? kEpiBF16Rope : kEpiBF16;
+  if (cos_sin && (head_dim != 64 && head_dim != 128)) return -13;
+  return gemm_entry(A, lda, 0, B, ldb, 0, D, ldd, epi, nullptr, 0, M, N, K, 1.0f, err, bn, 0,
+                    pos, cos_sin, rope_cols, head_dim, tp, st);
 }

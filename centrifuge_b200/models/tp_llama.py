@@ -107,6 +107,11 @@ class TPLlamaCore(torch.nn.Module):
         self.replicated = replicated_names(self.flat.names())
         self.pending_input_grad = None
         self.last_state = None
+        # Forward collectives fused with RMSNorm / the GEMMs over NVLink (parallel/tp_fused.py).
+        # The gather buffers double as saved activations until the next forward, so this is for
+        # schedules with one micro-batch in flight (no pipeline interleaving).
+        self.use_fused_comm = False
+        self._comm = None
 
     def reduce_replicated_grads(self) -> None:
         """Sum the gradients of replicated weights (embedding, RMSNorm) over the TP group.
@@ -152,6 +157,9 @@ class TPLlamaCore(torch.nn.Module):
             x = fused.embedding_fwd(p["embed"], sv["ids_local"])
         else:
             x = hidden_in.contiguous()
+        comm = self._fused_comm(T) if (self.use_fused_comm and P > 1) else None
+        if comm is not None:
+            return self._forward_fused(comm, x, input_ids, labels, B, S, sv, pos)
         for i in self.layer_ids:
             pre = f"layers.{i}."
             L = {"x": x}
@@ -175,6 +183,10 @@ class TPLlamaCore(torch.nn.Module):
         xf_p, rf = fused.rmsnorm_fwd(x, p["norm"], cfg.rms_norm_eps)
         xf = tp.all_gather_rows(xf_p)
         logits = G.linear_fwd(xf, p["lm_head"])
+        return self._head_loss(logits, x, xf, rf, input_ids, labels, B, S, sv)
+
+    def _head_loss(self, logits, x, xf, rf, input_ids, labels, B, S, sv):
+        tp, P = self.tp, self.tp.size
         if labels is None:
             lab = torch.full((B, S), -100, dtype=torch.long, device=x.device)
             lab[:, :-1] = input_ids[:, 1:]
@@ -192,6 +204,39 @@ class TPLlamaCore(torch.nn.Module):
             loss, lse_ce = fused.ce_fwd(logits, lab)
         sv["head"] = dict(x=x, xf=xf, rstdf=rf, logits=logits, labels=lab, lse=lse_ce)
         return loss.view(B, S)[:, :-1].contiguous(), sv
+
+    def _fused_comm(self, T: int):
+        if self._comm is None or self._comm.T != T:
+            from ..parallel.tp_fused import TPFusedComm
+            self._comm = TPFusedComm(self.tp, T, self.cfg.hidden_size,
+                                     2 * len(self.layer_ids) + 1, self.device)
+        return self._comm
+
+    def _forward_fused(self, comm, x, input_ids, labels, B, S, sv, pos):
+        """Forward with the sequence-parallel all-gathers fused into RMSNorm + the consuming
+        GEMM and the reduce-scatters fused into the row-parallel GEMMs (parallel/tp_fused.py)."""
+        p, cfg, tp = self.flat.params, self.cfg, self.tp
+        nh, nkv, hd = self.nh, self.nkv, self.hd
+        eps = cfg.rms_norm_eps
+        for li, i in enumerate(self.layer_ids):
+            pre = f"layers.{i}."
+            L = {"x": x}
+            xn, r1, e1 = comm.rmsnorm_push(x, p[pre + "ln1"], eps, 2 * li)
+            qkv = comm.gemm_ag(xn, p[pre + "wqkv"], e1,
+                               rope=(pos, self._rope, (nh + nkv) * hd, hd))
+            o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd, scale=self.scale)
+            x2 = comm.gemm_rs(o, p[pre + "wo"], x)
+            xn2, r2, e2 = comm.rmsnorm_push(x2, p[pre + "ln2"], eps, 2 * li + 1)
+            gu = comm.gemm_ag(xn2, p[pre + "wgu"], e2)
+            h = fused.swiglu_fwd(gu)
+            x = comm.gemm_rs(h, p[pre + "wd"], x2)
+            L.update(xn=xn, rstd1=r1, qkv=qkv, o=o, lse=lse, x2=x2, xn2=xn2, rstd2=r2, gu=gu, h=h)
+            sv["layers"].append(L)
+        if not self.has_head:
+            return x, sv
+        xf, rf, ef = comm.rmsnorm_push(x, p["norm"], eps, 2 * len(self.layer_ids))
+        logits = comm.gemm_ag(xf, p["lm_head"], ef)
+        return self._head_loss(logits, x, xf, rf, input_ids, labels, B, S, sv)
 
     # ------------------------------------------------------------------ backward
     def _backward_impl(self, sv, grad_out, state: Optional[FilterState]):
