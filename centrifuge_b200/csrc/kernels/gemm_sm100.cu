@@ -37,12 +37,14 @@ struct GemmArgs {
   const int* pos;
   const float* cs;
   int rope_cols, hd;
-  // ---- tensor-parallel fusion (sequence-parallel row shards of shard_mblocks 128-row blocks)
-  int rank, P, shard_mblocks;
+  // ---- tensor-parallel fusion.  Row segments: rank q owns rows [seg[q], seg[q+1]) of A / D
+  // (device array [P + 1]; uniform shards in the forward, kept rows in the backward)
+  int rank, P;
+  const int* seg;
   uint32_t epoch;
-  // all-gather consumer (TPM 1): A rows of shard s are usable once a_ready[s] >= epoch (local
-  // flags raised by the producer of each shard); m-blocks are rotated by rot_mblocks so the
-  // rank's own shard, ready first, is computed first
+  // all-gather consumer (TPM 1): A rows of segment q are usable once a_ready[q] >= epoch (local
+  // flags raised by the producer of each segment); m-blocks are rotated by rot_mblocks so the
+  // rank's own segment, ready first, is computed first
   const uint32_t* a_ready;
   int rot_mblocks;
   // reduce-scatter producer (TPM 2): D is this rank's partial-sum buffer (symmetric memory);
@@ -54,8 +56,9 @@ struct GemmArgs {
   const __nv_bfloat16* mc_part;            // multicast address of D, or nullptr
   const __nv_bfloat16* const* peer_part;   // D of every rank (peer loads when no multicast)
   const __nv_bfloat16* rs_resid;           // [shard rows, N] added to the reduced rows
-  __nv_bfloat16* rs_out;                   // [shard rows, N] reduced rows of this rank
+  __nv_bfloat16* rs_out;                   // [out_rows, N] reduced rows of this rank, then zeros
   long long ld_resid, ld_out;
+  int out_rows;
 };
 
 namespace tpc {
@@ -188,16 +191,18 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
         tile_coords(tile, num_m, num_n, tm, tn);
         if (TPM == 1) {
           tm = (tm + p.rot_mblocks) % num_m;
-          const int sh = tm / p.shard_mblocks;
-          if (!((ready_mask >> sh) & 1ull)) {
-            if (!tpc::wait_epoch(p.a_ready + sh, 1, p.epoch, abort_flag, p.err)) {
-              ok = false;
-              break;
-            }
-            // rows written by peers' generic stores are read below by the TMA (async proxy)
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-            ready_mask |= 1ull << sh;
+          // wait for every segment that intersects this m-block
+          const int r0 = tm * S::BM, r1 = min(p.M, r0 + S::BM);
+          bool waited = false;
+          for (int q = 0; q < p.P && ok; ++q) {
+            if (((ready_mask >> q) & 1ull) || p.seg[q] >= r1 || p.seg[q + 1] <= r0) continue;
+            if (!tpc::wait_epoch(p.a_ready + q, 1, p.epoch, abort_flag, p.err)) ok = false;
+            ready_mask |= 1ull << q;
+            waited = true;
           }
+          if (!ok) break;
+          // rows written by peers' generic stores are read below by the TMA (async proxy)
+          if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
         const int m0 = tm * S::BM, n0 = tn * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -296,6 +301,12 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
         okw = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_done, p.P, p.epoch - 2, abort_flag,
                               p.err);
       (void)__shfl_sync(0xffffffffu, okw ? 1 : 0, 0);  // on timeout abort_flag is raised
+      if (blockIdx.x == 0 && warp == 2 && lane == 0 && okw) {
+        // owners of empty segments receive nothing from this rank: tell them at once
+        for (int o = 0; o < p.P; ++o)
+          if (p.seg[o + 1] <= p.seg[o])
+            tpc::st_release_sys(p.peer_flags[o] + p.flag_ready + p.rank, p.epoch);
+      }
     }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       if (TPM == 2 && *abort_flag) break;
@@ -403,13 +414,20 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
       if (TPM == 2 && lane == 0) {
-        // count this warp's quarter of the tile; the last of a shard's tiles tells its owner
-        const int sh = tm / p.shard_mblocks;
-        const int sh_tiles = min(p.shard_mblocks, num_m - sh * p.shard_mblocks) * num_n;
-        __threadfence_system();
-        if (atomicAdd(p.tile_cnt + sh, 1u) == static_cast<uint32_t>(4 * sh_tiles - 1)) {
+        // this warp stored rows [c0, c0 + 32) of the tile: count the 32-row chunk for every
+        // owner segment it intersects; the last chunk of a segment tells its owner
+        const int c0 = m0 + row_in_tile - lane;
+        if (c0 < p.M) {
           __threadfence_system();
-          tpc::st_release_sys(p.peer_flags[sh] + p.flag_ready + p.rank, p.epoch);
+          for (int o = 0; o < p.P; ++o) {
+            const int lo = p.seg[o], hi = p.seg[o + 1];
+            if (hi <= lo || lo >= c0 + 32 || hi <= c0) continue;
+            const uint32_t need = static_cast<uint32_t>(((hi + 31) / 32 - lo / 32) * num_n);
+            if (atomicAdd(p.tile_cnt + o, 1u) == need - 1u) {
+              __threadfence_system();
+              tpc::st_release_sys(p.peer_flags[o] + p.flag_ready + p.rank, p.epoch);
+            }
+          }
         }
       }
     }
@@ -423,16 +441,20 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
       ok = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_ready, p.P, p.epoch, abort_flag, p.err);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     if (ok) {
-      const int shard_rows = p.shard_mblocks * S::BM;
-      const int r_lo = p.rank * shard_rows;
-      const int rows = max(0, min(p.M - r_lo, shard_rows));
+      const int r_lo = p.seg[p.rank];
+      const int rows = p.seg[p.rank + 1] - r_lo;  // reduced rows; rows..out_rows-1 are zeroed
       const int vec_per_row = p.N / 8;
-      const long long total = static_cast<long long>(rows) * vec_per_row;
+      const long long total = static_cast<long long>(p.out_rows) * vec_per_row;
       const int t = (warp - 6) * 32 + lane;
       for (long long v = static_cast<long long>(blockIdx.x) * 64 + t; v < total;
            v += static_cast<long long>(gridDim.x) * 64) {
         const int r = static_cast<int>(v / vec_per_row);
         const int c = static_cast<int>(v % vec_per_row) * 8;
+        if (r >= rows) {
+          *reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c) =
+              make_uint4(0u, 0u, 0u, 0u);
+          continue;
+        }
         const long long off = static_cast<long long>(r_lo + r) * p.ldd + c;
         float acc[8];
         if (p.mc_part) {
@@ -643,7 +665,8 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.hd = hd;
   a.rank = 0;
   a.P = 1;
-  a.shard_mblocks = 1;
+  a.seg = nullptr;
+  a.out_rows = 0;
   a.epoch = 0;
   a.a_ready = nullptr;
   a.rot_mblocks = 0;
@@ -657,29 +680,28 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.ld_resid = a.ld_out = 0;
   if (tp) {
     if (tp->mode != 1 && tp->mode != 2) return -13;
-    if (a_mn || b_mn) return -13;  // forward / dgrad-as-forward layouts only
-    if (tp->shard_rows % 128 || tp->P < 1 || tp->P > 64 || M > tp->P * tp->shard_rows)
-      return -13;
+    if (a_mn) return -13;  // rows of A are the sequence-parallel rows
+    if (tp->P < 1 || tp->P > 64 || !tp->seg || tp->rot_rows % 128) return -13;
     a.rank = tp->rank;
     a.P = tp->P;
-    a.shard_mblocks = tp->shard_rows / 128;
+    a.seg = tp->seg;
     a.epoch = tp->epoch;
     if (tp->mode == 1) {
       if (!tp->a_ready) return -13;
       a.a_ready = tp->a_ready;
-      a.rot_mblocks = tp->rank * a.shard_mblocks;
+      a.rot_mblocks = tp->rot_rows / 128;
+#define CFB_TP1(BNV, BMN, E) launch_gemm<BNV, false, BMN, E, 1>(ta, tb, a, st, max_ctas)
       if (epi == kEpiBF16) {
-        return bn == 256 ? launch_gemm<256, false, false, kEpiBF16, 1>(ta, tb, a, st, max_ctas)
-                         : launch_gemm<128, false, false, kEpiBF16, 1>(ta, tb, a, st, max_ctas);
+        if (b_mn) return bn == 256 ? CFB_TP1(256, true, kEpiBF16) : CFB_TP1(128, true, kEpiBF16);
+        return bn == 256 ? CFB_TP1(256, false, kEpiBF16) : CFB_TP1(128, false, kEpiBF16);
       }
-      if (epi == kEpiBF16Rope) {
-        return bn == 256 ? launch_gemm<256, false, false, kEpiBF16Rope, 1>(ta, tb, a, st, max_ctas)
-                         : launch_gemm<128, false, false, kEpiBF16Rope, 1>(ta, tb, a, st, max_ctas);
-      }
+      if (epi == kEpiBF16Rope && !b_mn)
+        return bn == 256 ? CFB_TP1(256, false, kEpiBF16Rope) : CFB_TP1(128, false, kEpiBF16Rope);
+#undef CFB_TP1
       return -4;
     }
     if (epi != kEpiBF16 || !tp->peer_flags || !tp->tile_cnt || !tp->out ||
-        (!tp->mc_part && !tp->peer_part) || (N % 8))
+        (!tp->mc_part && !tp->peer_part) || (N % 8) || tp->out_rows < 0)
       return -13;
     a.peer_flags = tp->peer_flags;
     a.flag_ready = tp->flag_ready;
@@ -691,8 +713,11 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
     a.rs_out = static_cast<__nv_bfloat16*>(tp->out);
     a.ld_resid = tp->ld_resid;
     a.ld_out = tp->ld_out;
-    return bn == 256 ? launch_gemm<256, false, false, kEpiBF16, 2>(ta, tb, a, st, max_ctas)
-                     : launch_gemm<128, false, false, kEpiBF16, 2>(ta, tb, a, st, max_ctas);
+    a.out_rows = tp->out_rows;
+#define CFB_TP2(BNV, BMN) launch_gemm<BNV, false, BMN, kEpiBF16, 2>(ta, tb, a, st, max_ctas)
+    if (b_mn) return bn == 256 ? CFB_TP2(256, true) : CFB_TP2(128, true);
+    return bn == 256 ? CFB_TP2(256, false) : CFB_TP2(128, false);
+#undef CFB_TP2
   }
   if (bn == 256) return dispatch_epi<256>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
   return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
@@ -717,13 +742,13 @@ int cfb_gemm_bf16_rope(const void* A, long long lda, const void* B, long long ld
                     bn, max_ctas, pos, cos_sin, rope_cols, head_dim, nullptr, st);
 }
 
-int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, void* D,
+int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,
                 long long ldd, int M, int N, int K, const int* pos, const float* cos_sin,
                 int rope_cols, int head_dim, const CfbTpGemm* tp, int* err, int bn,
                 cudaStream_t st) {
   if (!tp) return -13;
   const int epi = cos_sin ? kEpiBF16Rope : kEpiBF16;
   if (cos_sin && (head_dim != 64 && head_dim != 128)) return -13;
-  return gemm_entry(A, lda, 0, B, ldb, 0, D, ldd, epi, nullptr, 0, M, N, K, 1.0f, err, bn, 0,
+  return gemm_entry(A, lda, 0, B, ldb, b_mn, D, ldd, epi, nullptr, 0, M, N, K, 1.0f, err, bn, 0,
                     pos, cos_sin, rope_cols, head_dim, tp, st);
 }

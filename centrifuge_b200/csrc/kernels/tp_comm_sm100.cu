@@ -30,13 +30,12 @@ __device__ __forceinline__ void multimem_st16(void* mc, uint4 v) {
                : "memory");
 }
 
-// Warp per row of the local shard.  Row r of the shard goes to row (rank * shard_rows + r) of
-// the gather buffer.
+// Warp per row of the local rows.  Row r goes to row (row_base + r) of the gather buffer.
 __global__ void __launch_bounds__(256) rmsnorm_push_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, int rows, int H,
     float eps, __nv_bfloat16* mc_dst, __nv_bfloat16* const* peer_dst, long long ld_dst,
     float* __restrict__ rstd, uint32_t* const* peer_flags, int flag_off, int rank, int P,
-    int shard_rows, uint32_t epoch, uint32_t* cnt) {
+    int row_base, uint32_t epoch, uint32_t* cnt) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row < rows) {
@@ -54,7 +53,7 @@ __global__ void __launch_bounds__(256) rmsnorm_push_kernel(
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / static_cast<float>(H) + eps);
     if (lane == 0) rstd[row] = r;
-    const long long drow = static_cast<long long>(rank) * shard_rows + row;
+    const long long drow = static_cast<long long>(row_base) + row;
     for (int c = lane * 8; c < H; c += 256) {
       const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
       const uint4 g = *reinterpret_cast<const uint4*>(w + c);
@@ -94,13 +93,12 @@ __global__ void __launch_bounds__(256) rmsnorm_push_kernel(
 int cfb_tp_rmsnorm_push(const void* x, const void* w, int rows, int H, float eps, void* mc_dst,
                         void* const* peer_dst, long long ld_dst, float* rstd,
                         uint32_t* const* peer_flags, int flag_off, int rank, int P,
-                        int shard_rows, uint32_t epoch, uint32_t* cnt, cudaStream_t st) {
-  if (H % 8 || ld_dst % 8 || rows > shard_rows || (!mc_dst && !peer_dst) || !peer_flags || !cnt)
-    return -11;
+                        int row_base, uint32_t epoch, uint32_t* cnt, cudaStream_t st) {
+  if (H % 8 || ld_dst % 8 || (!mc_dst && !peer_dst) || !peer_flags || !cnt) return -11;
   const int grid = rows > 0 ? (rows + 7) / 8 : 1;
   cfb::tpcomm::rmsnorm_push_kernel<<<grid, 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(w), rows, H, eps,
       static_cast<__nv_bfloat16*>(mc_dst), reinterpret_cast<__nv_bfloat16* const*>(peer_dst),
-      ld_dst, rstd, peer_flags, flag_off, rank, P, shard_rows, epoch, cnt);
+      ld_dst, rstd, peer_flags, flag_off, rank, P, row_base, epoch, cnt);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -208,8 +208,9 @@ class TPLlamaCore(torch.nn.Module):
     def _fused_comm(self, T: int):
         if self._comm is None or self._comm.T != T:
             from ..parallel.tp_fused import TPFusedComm
+            # slots: xn, xn2 per layer, the final norm, two for the backward's gathers
             self._comm = TPFusedComm(self.tp, T, self.cfg.hidden_size,
-                                     2 * len(self.layer_ids) + 1, self.device)
+                                     2 * len(self.layer_ids) + 3, self.device)
         return self._comm
 
     def _forward_fused(self, comm, x, input_ids, labels, B, S, sv, pos):
@@ -232,6 +233,7 @@ class TPLlamaCore(torch.nn.Module):
             x = comm.gemm_rs(h, p[pre + "wd"], x2)
             L.update(xn=xn, rstd1=r1, qkv=qkv, o=o, lse=lse, x2=x2, xn2=xn2, rstd2=r2, gu=gu, h=h)
             sv["layers"].append(L)
+        sv["fused"] = True
         if not self.has_head:
             return x, sv
         xf, rf, ef = comm.rmsnorm_push(x, p["norm"], eps, 2 * len(self.layer_ids))
@@ -251,6 +253,8 @@ class TPLlamaCore(torch.nn.Module):
             rows, Sk, pos_flat, pos2d = None, S, self._pos(B, S), None
         Tk, H = B * Sk, cfg.hidden_size
         local = None if lay.identity else lay.local
+        if sv.get("fused") and tp.size > 1:
+            return self._backward_fused(sv, grad_out, state, lay, rows, Sk, pos_flat, pos2d)
 
         def ag(dx_p):  # padded local kept rows -> compact global kept rows
             return lay.to_compact(tp.all_gather_rows(dx_p), _gather)
@@ -324,6 +328,94 @@ class TPLlamaCore(torch.nn.Module):
         if self.has_embed:
             return None
         return dx
+
+
+def _backward_fused_impl(self, sv, grad_out, state, lay, rows, Sk, pos_flat, pos2d):
+    """Filtered backward with the all-gathers fused into the RMSNorm backward + the consuming
+    dgrad GEMM and the reduce-scatters fused into the column-parallel dgrad GEMMs.  Kept rows
+    stay in the compact global order: rank q's kept rows are rows [start_q, start_q + count_q)
+    of every gathered tensor and of every partial sum (rank-major because shards are row
+    ranges), so the GEMMs see exactly the kept rows; local rows keep the padded layout of
+    :class:`KeptLayout` (C rows, zero padding)."""
+    from ..parallel.tp_fused import Segments
+    p, g, cfg, tp = self.flat.params, self.flat.grads, self.cfg, self.tp
+    comm = self._comm
+    B, S = sv["B"], sv["S"]
+    nh, nkv, hd = self.nh, self.nkv, self.hd
+    seg = Segments(lay.counts, self.device)
+    C = lay.C
+    local = None if lay.identity else lay.local
+    slot_a = 2 * len(self.layer_ids) + 1
+    slot_b = slot_a + 1
+
+    def gat(t):
+        return t if rows is None else _gather(t, rows)
+
+    assert self.has_head, "the fused backward runs on a full TP model (no pipeline stages)"
+    hd_ = sv["head"]
+    dl = grad_out.float()
+    if state is not None and dl.shape[1] == S - 1:
+        dl = torch.gather(dl, 1, pos2d[:, :-1].long())
+    dl = torch.cat([dl, torch.zeros(B, 1, device=dl.device, dtype=dl.dtype)], 1)
+    dloss = dl.reshape(-1).contiguous()
+    dlogits = fused.ce_bwd(hd_["logits"], hd_["labels"], hd_["lse"], dloss, rows,
+                           vocab_start=self.vocab_start)
+    xf_k = gat(hd_["xf"])
+    G.linear_wgrad(dlogits, xf_k, g["lm_head"])
+    dxf_p = comm.gemm_rs(dlogits, p["lm_head"], None, seg=seg, b_mn=True, out_rows=C)
+    del dlogits, xf_k
+    layers = list(enumerate(self.layer_ids))
+    # dx of the final norm, gathered for the last layer's down projection
+    dx, dYg, ea = comm.rmsnorm_bwd_push(dxf_p, hd_["x"], hd_["rstdf"], p["norm"], g["norm"],
+                                        local, None, slot_a, seg)
+    for li, i in reversed(layers):
+        L = sv["layers"][li]
+        pre = f"layers.{i}."
+        # ---- MLP: dgrad first (it waits for the gathered rows), then wgrad
+        dh = comm.gemm_ag(dYg, p[pre + "wd"], ea, seg=seg, b_mn=True)
+        h_k = gat(L["h"])
+        G.linear_wgrad(dYg, h_k, g[pre + "wd"])
+        del h_k
+        dgu = fused.swiglu_bwd(dh, L["gu"], rows)
+        del dh
+        xn2_k = gat(L["xn2"])
+        G.linear_wgrad(dgu, xn2_k, g[pre + "wgu"])
+        dxn2_p = comm.gemm_rs(dgu, p[pre + "wgu"], None, seg=seg, b_mn=True, out_rows=C)
+        del dgu, xn2_k
+        dx2, dY2g, eb = comm.rmsnorm_bwd_push(dxn2_p, L["x2"], L["rstd2"], p[pre + "ln2"],
+                                              g[pre + "ln2"], local, dx, slot_b, seg)
+        del dxn2_p, dx
+        # ---- attention
+        do = comm.gemm_ag(dY2g, p[pre + "wo"], eb, seg=seg, b_mn=True)
+        o_k = gat(L["o"])
+        G.linear_wgrad(dY2g, o_k, g[pre + "wo"])
+        qkv_k = gat(L["qkv"])
+        lse_k = L["lse"] if rows is None else _gather(L["lse"], rows)
+        dqkv = fused.attn_bwd(qkv_k, L["qkv"], o_k, do, lse_k,
+                              pos2d if pos2d is not None else pos_flat.view(B, S),
+                              B, S, Sk, nh, nkv, hd, scale=self.scale, rope_table=self._rope)
+        del qkv_k, lse_k, o_k, do
+        xn_k = gat(L["xn"])
+        G.linear_wgrad(dqkv, xn_k, g[pre + "wqkv"])
+        dxn_p = comm.gemm_rs(dqkv, p[pre + "wqkv"], None, seg=seg, b_mn=True, out_rows=C)
+        del dqkv, xn_k
+        if li > 0:
+            dx, dYg, ea = comm.rmsnorm_bwd_push(dxn_p, L["x"], L["rstd1"], p[pre + "ln1"],
+                                                g[pre + "ln1"], local, dx2, slot_a, seg)
+        else:
+            dx = fused.rmsnorm_bwd(dxn_p, L["x"], L["rstd1"], p[pre + "ln1"], g[pre + "ln1"],
+                                   x_rows=local, dres=dx2)
+        del dxn_p, dx2
+        sv["layers"][li] = None
+    if self.has_embed:
+        n = lay.count if not lay.identity else dx.shape[0]
+        fused.embedding_bwd(dx[:n], sv["ids_local"], g["embed"],
+                            id_rows=None if lay.identity else lay.local[:n])
+        return None
+    return dx
+
+
+TPLlamaCore._backward_fused = _backward_fused_impl
 
 
 class _CfTPLlamaFn(torch.autograd.Function):

@@ -62,7 +62,7 @@ class KeptLayout:
       ``local``     [C]     this rank's kept rows as shard-local indices, padded with 0
       ``c2p``       [Tk]    compact index -> padded slot (owner * C + j)
       ``p2c``       [P*C]   padded slot -> compact index, or Tk for padding (a zero row)
-      ``C``, ``count`` (this rank's real kept rows), ``Tk``
+      ``C``, ``count`` (this rank's real kept rows), ``Tk``, ``counts`` (host list, per rank)
     """
 
     def __init__(self, rows: Optional[torch.Tensor], T: int, tp: TPGroup, device):
@@ -76,6 +76,7 @@ class KeptLayout:
             self.local = torch.arange(shard, **i32)
             self.c2p = self.rows
             self.p2c = self.rows
+            self.counts = [shard] * P
             self.identity = True
             return
         self.identity = False
@@ -94,6 +95,7 @@ class KeptLayout:
         mine = rows[owner == p] - p * shard
         local[:mine.numel()] = mine
         self.rows = rows.to(torch.int32)
+        self.counts = cvals
         self.Tk, self.C, self.count = Tk, C, cvals[p]
         self.local = local.to(torch.int32)
         self.c2p = c2p.to(torch.int32)

@@ -70,6 +70,7 @@ class TPFusedComm:
         self.push_cnt = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ag_epoch = 0
         self.rs_epoch = 0
+        self._uniform = None
         torch.cuda.synchronize(self.device)
         import torch.distributed as dist
         dist.barrier(tp.group)
@@ -80,50 +81,102 @@ class TPFusedComm:
 
     def gather_view(self, slot: int, rows: Optional[int] = None) -> torch.Tensor:
         T, H = self.T, self.H
-        return self.gbuf[slot * T * H:(slot + 1) * T * H].view(T, H)[: (rows or T)]
+        return self.gbuf[slot * T * H:(slot + 1) * T * H].view(T, H)[: (T if rows is None else rows)]
 
-    # ---------------------------------------------------------------- all-gather
+    def uniform_segments(self) -> "Segments":
+        if self._uniform is None:
+            counts = [self.shard] * self.P
+            self._uniform = Segments(counts, self.device)
+        return self._uniform
+
+    def _mc(self, base: int, slot_elems: int) -> int:
+        return base + slot_elems * 2 if base else 0
+
+    # ---------------------------------------------------------------- all-gather producers
     def rmsnorm_push(self, x_local: torch.Tensor, w: torch.Tensor, eps: float,
                      slot: int) -> Tuple[torch.Tensor, torch.Tensor, int]:
-        """RMSNorm of the local rows, gathered into slot ``slot`` of every rank.
+        """RMSNorm of the local shard (uniform segments), gathered into slot ``slot``.
 
-        Returns ``(gathered [T, H] view, rstd [rows], epoch)``; the gathered rows are complete
+        Returns ``(gathered [T, H] view, rstd [shard], epoch)``; the gathered rows are complete
         only for a consumer that waits on ``epoch`` (:meth:`gemm_ag`)."""
         assert x_local.shape[0] == self.shard and x_local.shape[1] == self.H
         self.ag_epoch += 1
         rstd = torch.empty(self.shard, dtype=torch.float32, device=self.device)
         T, H = self.T, self.H
-        mc = self.g_mc + slot * T * H * 2 if self.g_mc else 0
-        kernels().tp_rmsnorm_push(x_local, w, eps, mc, self.g_peers[slot].data_ptr(), H, rstd,
-                                  self.peer_flags_dev, 0, self.rank, self.P, self.shard,
-                                  self.ag_epoch, self.push_cnt)
+        kernels().tp_rmsnorm_push(x_local, w, eps, self._mc(self.g_mc, slot * T * H),
+                                  self.g_peers[slot].data_ptr(), H, rstd, self.peer_flags_dev, 0,
+                                  self.rank, self.P, self.rank * self.shard, self.ag_epoch,
+                                  self.push_cnt)
         return self.gather_view(slot), rstd, self.ag_epoch
 
+    def rmsnorm_bwd_push(self, dy, x, rstd, w, dw_acc, x_rows, dres, slot: int,
+                         seg: "Segments") -> Tuple[torch.Tensor, torch.Tensor, int]:
+        """RMSNorm backward of the local (padded) rows whose first ``count`` output rows are also
+        gathered into slot ``slot`` at this rank's segment.  Returns ``(dx [rows, H],
+        gathered [Tk, H] view, epoch)``."""
+        self.ag_epoch += 1
+        T, H = self.T, self.H
+        dx = torch.empty_like(dy)
+        partial_rows = max(1, min(dy.shape[0], 148 * 2))
+        kernels().tp_rmsnorm_bwd_push(dy, x, x_rows, rstd, w, dres, dx, dw_acc, partial_rows,
+                                      self._mc(self.g_mc, slot * T * H),
+                                      self.g_peers[slot].data_ptr(), H, seg.start[self.rank],
+                                      seg.counts[self.rank], self.peer_flags_dev, 0, self.rank,
+                                      self.P, self.ag_epoch, self.push_cnt)
+        return dx, self.gather_view(slot, seg.total), self.ag_epoch
+
+    # ---------------------------------------------------------------- consumers / producers
     def gemm_ag(self, xg: torch.Tensor, w: torch.Tensor, epoch: int,
                 rope: Optional[Tuple[torch.Tensor, torch.Tensor, int, int]] = None,
+                seg: Optional["Segments"] = None, b_mn: bool = False,
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """``xg @ w^T`` where ``xg`` is a gathered slot filled by :meth:`rmsnorm_push`."""
+        """``xg @ w^T`` (``xg @ w`` with ``b_mn``) where ``xg`` is a gathered slot, waiting per
+        source segment inside the kernel."""
+        seg = seg or self.uniform_segments()
+        N = w.shape[1] if b_mn else w.shape[0]
         if out is None:
-            out = torch.empty(xg.shape[0], w.shape[0], dtype=xg.dtype, device=self.device)
+            out = torch.empty(xg.shape[0], N, dtype=xg.dtype, device=self.device)
+        if xg.shape[0] == 0:
+            return out
         pos, table, rc, hd = rope if rope is not None else (None, None, 0, 0)
-        kernels().gemm_tp(xg, w, out, pos, table, rc, hd, 1, self.rank, self.P, self.shard,
-                          epoch, self.ag_ready, 0, 0, 0, None, 0, 0, None, None)
+        rot = (seg.start[self.rank] // 128) * 128
+        kernels().gemm_tp(xg, w, out, b_mn, pos, table, rc, hd, 1, self.rank, self.P, seg.dev,
+                          epoch, self.ag_ready, rot, 0, 0, 0, None, 0, 0, None, None)
         return out
 
-    # ---------------------------------------------------------------- reduce-scatter
     def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, resid: Optional[torch.Tensor],
-                out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """This rank's rows of ``sum_ranks(a @ w^T)`` (+ ``resid``), ``[shard, N]``."""
-        T, N = a.shape[0], w.shape[0]
-        assert T == self.T and N <= self.H
+                seg: Optional["Segments"] = None, b_mn: bool = False,
+                out_rows: Optional[int] = None, out: Optional[torch.Tensor] = None
+                ) -> torch.Tensor:
+        """This rank's segment of ``sum_ranks(a @ w^T)`` (``a @ w`` with ``b_mn``) plus
+        ``resid``, as ``[out_rows, N]`` (rows past the segment are zero)."""
+        seg = seg or self.uniform_segments()
+        T = a.shape[0]
+        N = w.shape[1] if b_mn else w.shape[0]
+        assert T == seg.total and T <= self.T and N <= self.H
         self.rs_epoch += 1
         e = self.rs_epoch
         i = e & 1
-        part = self.pbuf[i * self.T * self.H:i * self.T * self.H + T * N].view(T, N)
+        part = self.pbuf[i * self.T * self.H:i * self.T * self.H + max(T, 1) * N].view(-1, N)[:T]
+        rows = seg.counts[self.rank] if out_rows is None else out_rows
         if out is None:
-            out = torch.empty(self.shard, N, dtype=a.dtype, device=self.device)
-        mc = self.p_mc + i * self.T * self.H * 2 if self.p_mc else 0
-        kernels().gemm_tp(a, w, part, None, None, 0, 0, 2, self.rank, self.P, self.shard, e, 0,
-                          self.peer_flags_dev, self.off_rs_ready, self.off_rs_done, self.cnt,
-                          mc, self.p_peers[i].data_ptr(), resid, out)
+            out = torch.empty(rows, N, dtype=a.dtype, device=self.device)
+        kernels().gemm_tp(a, w, part, b_mn, None, None, 0, 0, 2, self.rank, self.P, seg.dev, e, 0,
+                          0, self.peer_flags_dev, self.off_rs_ready, self.off_rs_done, self.cnt,
+                          self._mc(self.p_mc, i * self.T * self.H), self.p_peers[i].data_ptr(),
+                          resid, out)
         return out
+
+
+class Segments:
+    """Per-rank row segments of a sequence-parallel tensor: rank q owns rows
+    ``[start[q], start[q] + counts[q])`` (host lists) and ``dev`` is the int32 device prefix
+    array ``[P + 1]`` the kernels read."""
+
+    def __init__(self, counts, device):
+        self.counts = [int(c) for c in counts]
+        self.start = [0]
+        for c in self.counts:
+            self.start.append(self.start[-1] + c)
+        self.total = self.start[-1]
+        self.dev = torch.tensor(self.start, dtype=torch.int32, device=device)

@@ -94,31 +94,47 @@ def _fused_worker(rank, world, port, q):
         for v in tp.flat.params.values():
             v.copy_(0.05 * torch.randn_like(v, dtype=torch.float32))
         g = torch.Generator().manual_seed(3)
-        B, S = 2, 256
+        B, S = 1, 512  # shards split the sequence: kept rows per rank differ
         ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g).cuda()
+        from centrifuge_b200.filter import backward_filter
+        from centrifuge_b200.loss import token_filter_loss
+        os.environ["CFB_NODE_TRACING_FILE"] = f"/tmp/cfb_tpf_dims_{rank}.txt"
+        rl = torch.exp(1.0 + 0.5 * torch.randn(B, S - 1, generator=g)).cuda()
         res = {}
-        for fused in (False, True, True):  # the second fused pass reuses buffers / epochs
+        # dense backward, filtered backward (kept rows per rank differ), and a repeat of both
+        for filt, fused in ((False, False), (False, True), (True, False), (True, True),
+                            (True, True), (False, True)):
             tp.use_fused_comm = fused
             tp.flat.grad.zero_()
             out = tp(ids).token_loss
-            loss = out.float().mean()
+            if filt:
+                loss, mask = token_filter_loss(ids, None,
+                                               torch.ones(B, S, dtype=torch.long, device="cuda"),
+                                               rl, "fixed", 0.5, True, True,
+                                               per_token_loss=out)
+                backward_filter(loss, mask)
+            else:
+                loss = out.float().mean()
             loss.backward()
             torch.cuda.synchronize()
-            res.setdefault(fused, []).append((float(loss.detach()), tp.flat.grad.clone()))
+            res.setdefault((filt, fused), []).append((float(loss.detach()), tp.flat.grad.clone()))
         err_word = kernels().gemm_error_word(rank, True)
-        l0, g0 = res[False][0]
         out = []
-        for l1, g1 in res[True]:
-            out.append((abs(l1 - l0) / abs(l0),
-                        float((g1 - g0).norm() / (g0.norm() + 1e-12))))
+        for filt in (False, True):
+            l0, g0 = res[(filt, False)][0]
+            for l1, g1 in res[(filt, True)]:
+                out.append((abs(l1 - l0) / abs(l0),
+                            float((g1 - g0).norm() / (g0.norm() + 1e-12))))
         q.put((rank, out, err_word, tp._comm.kind))
     finally:
         dist.destroy_process_group()
 
 
 def test_tp2_fused_collectives_match_nccl():
-    """Forward all-gathers fused into RMSNorm + the consuming GEMM and reduce-scatters fused into
-    the row-parallel GEMMs give the same loss and gradients as the NCCL path."""
+    """All-gathers fused into RMSNorm (forward and backward) + the consuming GEMM, and
+    reduce-scatters fused into the row-parallel (forward) and column-parallel dgrad (backward)
+    GEMMs give the same loss and gradients as the NCCL path, dense and with filtering (kept rows
+    per rank differ)."""
     import torch.multiprocessing as mp
 
     from tests.dist_utils import free_port
