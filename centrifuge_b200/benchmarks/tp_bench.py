@@ -35,6 +35,10 @@ def main():
     ap.add_argument("--drop", type=float, nargs="+", default=[0.5])
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="fused: collectives fused into RMSNorm / the GEMMs over NVLink "
+                         "(tensor-parallel without pipeline stages); nccl: NCCL all-gather / "
+                         "reduce-scatter (the baseline)")
     a = ap.parse_args()
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -60,6 +64,7 @@ def main():
     layers = stage_layers(cfg.num_hidden_layers, a.pp, g.stage)
     core = TPLlamaCore(cfg, g.tp_group, device=dev, first=layers.start, last=layers.stop,
                        has_embed=g.stage == 0, has_head=g.stage == a.pp - 1)
+    core.use_fused_comm = a.comm == "fused" and a.pp == 1 and a.tp > 1
     gen = torch.Generator(device=dev).manual_seed(1234 + g.stage * 100 + g.tp_rank)
     for name, p in core.flat.params.items():
         if p.dim() == 1:
@@ -104,6 +109,7 @@ def main():
                            "micro_batch": a.mbs, "micro_batches": M,
                            "global_batch": M * a.mbs,
                            "parallelism": f"tp{a.tp}" + (f"pp{a.pp}-1f1b" if a.pp > 1 else "-sp")},
+                "comm": (core._comm.kind if core._comm is not None else "nccl"),
                 "dtype": "bf16", "data": "synthetic"}), flush=True)
     dist.barrier()
     dist.destroy_process_group()

@@ -120,39 +120,17 @@ void gemm_rope(const Tensor& a, const Tensor& b, Tensor& out, const Tensor& pos,
                "gemm_rope");
 }
 
-// ---- tensor-parallel fusions (pointers into symmetric memory are raw device addresses)
-void tp_rmsnorm_push(const Tensor& x, const Tensor& w, double eps, int64_t mc_dst,
-                     int64_t peer_dst_dev, int64_t ld_dst, Tensor& rstd, int64_t peer_flags_dev,
-                     int64_t flag_off, int64_t rank, int64_t P, int64_t row_base,
-                     int64_t epoch, Tensor& cnt) {
-  check_bf16_2d(x, "x");
-  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && w.numel() == x.size(1), "x, w");
-  TORCH_CHECK(rstd.scalar_type() == at::kFloat && rstd.numel() >= x.size(0), "rstd");
-  TORCH_CHECK(cnt.scalar_type() == at::kInt && cnt.is_cuda(), "cnt int32");
-  const c10::cuda::CUDAGuard guard(x.device());
-  CFB_CHECK_RC(cfb_tp_rmsnorm_push(x.data_ptr(), w.data_ptr(), static_cast<int>(x.size(0)),
-                                   static_cast<int>(x.size(1)), static_cast<float>(eps),
-                                   reinterpret_cast<void*>(mc_dst),
-                                   reinterpret_cast<void* const*>(peer_dst_dev), ld_dst,
-                                   rstd.data_ptr<float>(),
-                                   reinterpret_cast<uint32_t* const*>(peer_flags_dev),
-                                   static_cast<int>(flag_off), static_cast<int>(rank),
-                                   static_cast<int>(P), static_cast<int>(row_base),
-                                   static_cast<uint32_t>(epoch),
-                                   reinterpret_cast<uint32_t*>(cnt.data_ptr<int>()),
-                                   cur_stream()),
-               "tp_rmsnorm_push");
-}
-
-// out = a @ b^T fused with a tensor-parallel collective (mode 1: all-gather consumer of `a`;
-// mode 2: reduce-scatter producer, `out` is this rank's partial buffer and `rs_out` receives
-// the reduced own rows plus `resid`).  Optional RoPE epilogue (mode 1) with pos/table.
+// ---- tensor-parallel fusion (pointers into symmetric memory are raw device addresses)
+// out = a @ b^T (a @ b with b_mn) fused with a sequence-parallel collective over NVLink:
+// mode 1 all-gathers this rank's rows of `a` to every rank while computing, mode 2 stores the
+// partial rows into their owners' receive buffers and writes this rank's reduced rows (+resid)
+// into `rs_out` (`out` is then only a shape carrier and is not written).
 void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
              const c10::optional<Tensor>& pos, const c10::optional<Tensor>& table,
              int64_t rope_cols, int64_t hd, int64_t mode, int64_t rank, int64_t P,
-             const Tensor& seg, int64_t epoch, int64_t a_ready, int64_t rot_rows,
-             int64_t peer_flags_dev, int64_t flag_ready, int64_t flag_done,
-             const c10::optional<Tensor>& tile_cnt, int64_t mc_part, int64_t peer_part_dev,
+             const Tensor& seg, int64_t epoch, int64_t peer_flags_dev, int64_t flag_ready,
+             int64_t flag_done, Tensor& tile_cnt, int64_t rot_rows, int64_t ag_mc,
+             int64_t ag_peers_dev, int64_t recv_dev, int64_t seg_cap,
              const c10::optional<Tensor>& resid, const c10::optional<Tensor>& rs_out,
              int64_t bn) {
   check_bf16_2d(a, "a");
@@ -163,23 +141,22 @@ void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
               "gemm_tp: shapes");
   TORCH_CHECK(seg.is_cuda() && seg.scalar_type() == at::kInt && seg.numel() == P + 1,
               "gemm_tp: seg must be int32 [P + 1] on the device");
+  TORCH_CHECK(tile_cnt.scalar_type() == at::kInt && tile_cnt.numel() >= P + 2, "tile_cnt");
   CfbTpGemm t = {};
   t.mode = static_cast<int>(mode);
   t.rank = static_cast<int>(rank);
   t.P = static_cast<int>(P);
   t.seg = seg.data_ptr<int>();
   t.epoch = static_cast<uint32_t>(epoch);
-  t.a_ready = reinterpret_cast<const uint32_t*>(a_ready);
-  t.rot_rows = static_cast<int>(rot_rows);
   t.peer_flags = reinterpret_cast<uint32_t* const*>(peer_flags_dev);
   t.flag_ready = static_cast<int>(flag_ready);
   t.flag_done = static_cast<int>(flag_done);
-  if (tile_cnt.has_value() && tile_cnt->defined()) {
-    TORCH_CHECK(tile_cnt->scalar_type() == at::kInt && tile_cnt->numel() >= P + 2, "tile_cnt");
-    t.tile_cnt = reinterpret_cast<uint32_t*>(tile_cnt->data_ptr<int>());
-  }
-  t.mc_part = reinterpret_cast<const void*>(mc_part);
-  t.peer_part = reinterpret_cast<const void* const*>(peer_part_dev);
+  t.tile_cnt = reinterpret_cast<uint32_t*>(tile_cnt.data_ptr<int>());
+  t.rot_rows = static_cast<int>(rot_rows);
+  t.ag_mc = reinterpret_cast<void*>(ag_mc);
+  t.ag_peers = reinterpret_cast<void* const*>(ag_peers_dev);
+  t.recv = reinterpret_cast<void* const*>(recv_dev);
+  t.seg_cap = static_cast<int>(seg_cap);
   if (resid.has_value() && resid->defined()) {
     check_bf16_2d(*resid, "resid");
     t.resid = resid->data_ptr();
@@ -200,7 +177,6 @@ void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
     pp = pos->data_ptr<int>();
     cs = table->data_ptr<float>();
   }
-  if (M == 0 && mode == 1) return;
   const c10::cuda::CUDAGuard guard(a.device());
   CFB_CHECK_RC(cfb_gemm_tp(a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), b_mn ? 1 : 0,
                            out.data_ptr(), out.stride(0), static_cast<int>(M),
@@ -209,38 +185,6 @@ void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
                            err_word(a.get_device()).data_ptr<int>(), static_cast<int>(bn),
                            cur_stream()),
                "gemm_tp");
-}
-
-void tp_rmsnorm_bwd_push(const Tensor& dy, const Tensor& x, const c10::optional<Tensor>& x_rows,
-                         const Tensor& rstd, const Tensor& w, const c10::optional<Tensor>& dres,
-                         Tensor& dx, Tensor& dw_acc, int64_t partial_rows, int64_t mc_dst,
-                         int64_t peer_dst_dev, int64_t ld_dst, int64_t row_base, int64_t count,
-                         int64_t peer_flags_dev, int64_t flag_off, int64_t rank, int64_t P,
-                         int64_t epoch, Tensor& cnt) {
-  check_bf16_2d(dy, "dy");
-  check_bf16_2d(x, "x");
-  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dx.is_contiguous(), "contiguous");
-  TORCH_CHECK(dw_acc.scalar_type() == at::kFloat && dw_acc.is_contiguous(), "dw_acc fp32");
-  const int rows = dy.size(0), H = dy.size(1);
-  if (x_rows.has_value() && x_rows->defined())
-    TORCH_CHECK(x_rows->scalar_type() == at::kInt && x_rows->numel() == rows, "x_rows int32");
-  int Pp = static_cast<int>(std::min<int64_t>(partial_rows, std::max(rows, 1)));
-  if (Pp < 1) Pp = 1;
-  const c10::cuda::CUDAGuard guard(dy.device());
-  Tensor partial = at::empty({Pp, H}, dy.options().dtype(at::kFloat));
-  CFB_CHECK_RC(cfb_tp_rmsnorm_bwd_push(dy.data_ptr(), x.data_ptr(), opt_ptr<int>(x_rows),
-                                       rstd.data_ptr<float>(), w.data_ptr(),
-                                       opt_ptr<void>(dres), dx.data_ptr(),
-                                       partial.data_ptr<float>(), dw_acc.data_ptr<float>(), rows,
-                                       H, Pp, reinterpret_cast<void*>(mc_dst),
-                                       reinterpret_cast<void* const*>(peer_dst_dev), ld_dst,
-                                       static_cast<int>(row_base), static_cast<int>(count),
-                                       reinterpret_cast<uint32_t* const*>(peer_flags_dev),
-                                       static_cast<int>(flag_off), static_cast<int>(rank),
-                                       static_cast<int>(P), static_cast<uint32_t>(epoch),
-                                       reinterpret_cast<uint32_t*>(cnt.data_ptr<int>()),
-                                       cur_stream()),
-               "tp_rmsnorm_bwd_push");
 }
 
 int64_t gemm_error_word(int64_t device, bool reset) {
@@ -635,14 +579,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("resid") = py::none(),
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
-  m.def("tp_rmsnorm_push", &tp_rmsnorm_push);
   m.def("gemm_tp", &gemm_tp, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("b_mn"),
         py::arg("pos"), py::arg("table"), py::arg("rope_cols"), py::arg("hd"), py::arg("mode"),
-        py::arg("rank"), py::arg("P"), py::arg("seg"), py::arg("epoch"), py::arg("a_ready"),
-        py::arg("rot_rows"), py::arg("peer_flags_dev"), py::arg("flag_ready"),
-        py::arg("flag_done"), py::arg("tile_cnt"), py::arg("mc_part"), py::arg("peer_part_dev"),
-        py::arg("resid"), py::arg("rs_out"), py::arg("bn") = 0);
-  m.def("tp_rmsnorm_bwd_push", &tp_rmsnorm_bwd_push);
+        py::arg("rank"), py::arg("P"), py::arg("seg"), py::arg("epoch"),
+        py::arg("peer_flags_dev"), py::arg("flag_ready"), py::arg("flag_done"),
+        py::arg("tile_cnt"), py::arg("rot_rows"), py::arg("ag_mc"), py::arg("ag_peers_dev"),
+        py::arg("recv_dev"), py::arg("seg_cap"), py::arg("resid"), py::arg("rs_out"),
+        py::arg("bn") = 0);
   m.def("gemm_rope", &gemm_rope, "tcgen05 bf16 GEMM with RoPE fused into the epilogue",
         py::arg("a"), py::arg("b"), py::arg("out"), py::arg("pos"), py::arg("table"),
         py::arg("rope_cols"), py::arg("hd"), py::arg("bn") = 0);

@@ -163,45 +163,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
 // Warp per row: the lane owns NG groups of 8 columns, c = (lane + 32 g) * 8, and keeps their
 // dgamma partial sums in registers across the rows of its warp.  Pass 1 reads dy, x for the row
 // dot product; pass 2 re-reads them (L1-resident) to write dx.  No block barrier per row.
-// Optional all-gather push of the output (tensor-parallel backward): rows r < count are also
-// stored at row row_base + r of every rank's gather buffer (multicast address or each peer), and
-// when the grid is done ready[rank] = epoch is raised in every rank's flag buffer.
-struct BwdPush {
-  __nv_bfloat16* mc;
-  __nv_bfloat16* const* peers;
-  long long ld;
-  int row_base, count, rank, P, flag_off;
-  uint32_t* const* peer_flags;
-  uint32_t epoch;
-  uint32_t* cnt;
-};
-
-__device__ __forceinline__ void push_row16(const BwdPush& q, int r, int c, const float* o) {
-  uint4 v;
-  v.x = pack_bf16x2(o[0], o[1]);
-  v.y = pack_bf16x2(o[2], o[3]);
-  v.z = pack_bf16x2(o[4], o[5]);
-  v.w = pack_bf16x2(o[6], o[7]);
-  __nv_bfloat16* dst_off = nullptr;
-  const long long off = (static_cast<long long>(q.row_base) + r) * q.ld + c;
-  if (q.mc) {
-    dst_off = q.mc + off;
-    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst_off),
-                 "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
-                 "f"(__uint_as_float(v.w))
-                 : "memory");
-  } else {
-    for (int k = 0; k < q.P; ++k) *reinterpret_cast<uint4*>(q.peers[k] + off) = v;
-  }
-}
-
-template <int NG, bool PUSH = false>
+template <int NG>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
     const int* __restrict__ x_rows, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ dres,
-    __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_partial, int rows, int H,
-    BwdPush push = BwdPush{}) {
+    __nv_bfloat16* __restrict__ dx, float* __restrict__ dw_partial, int rows, int H) {
   const int lane = lane_id(), wp = warp_id();
   float dw[NG][8];
 #pragma unroll
@@ -250,7 +217,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] += rs * wv[i] * a[i] - b[i] * coef;
         store8(dx + static_cast<long long>(r) * H + c, o);
-        if (PUSH && r < push.count) push_row16(push, r, c, o);
       }
     }
   }
@@ -270,17 +236,6 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_warp_kernel(
       dw_partial[static_cast<long long>(blockIdx.x) * H + c] = t;
     }
     __syncthreads();
-  }
-  if (PUSH && threadIdx.x == 0) {
-    __threadfence_system();
-    if (atomicAdd(push.cnt, 1u) == gridDim.x - 1u) {
-      __threadfence_system();
-      for (int k = 0; k < push.P; ++k)
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(push.peer_flags[k] + push.flag_off + push.rank),
-                     "r"(push.epoch)
-                     : "memory");
-      atomicExch(push.cnt, 0u);
-    }
   }
 }
 
@@ -786,44 +741,6 @@ int cfb_rmsnorm_bwd(const void* dy, const void* x, const int* x_rows, const floa
       case 3: rmsnorm_bwd_kernel<3><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
       default: rmsnorm_bwd_kernel<4><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H); break;
     }
-  }
-  colsum_acc_kernel<<<(H + 31) / 32, 256, 0, st>>>(dw_partial, dw_acc, partial_rows, H);
-  return last_err();
-}
-
-int cfb_tp_rmsnorm_bwd_push(const void* dy, const void* x, const int* x_rows, const float* rstd,
-                            const void* w, const void* dres, void* dx, float* dw_partial,
-                            float* dw_acc, int rows, int H, int partial_rows, void* mc_dst,
-                            void* const* peer_dst, long long ld_dst, int row_base, int count,
-                            uint32_t* const* peer_flags, int flag_off, int rank, int P,
-                            uint32_t epoch, uint32_t* cnt, cudaStream_t st) {
-  if (H % 256 || H > 4096 || ld_dst % 8 || (!mc_dst && !peer_dst) || !peer_flags || !cnt ||
-      count > rows || partial_rows < 1)
-    return -11;
-  BwdPush q;
-  q.mc = static_cast<bf16*>(mc_dst);
-  q.peers = reinterpret_cast<bf16* const*>(peer_dst);
-  q.ld = ld_dst;
-  q.row_base = row_base;
-  q.count = count;
-  q.rank = rank;
-  q.P = P;
-  q.flag_off = flag_off;
-  q.peer_flags = peer_flags;
-  q.epoch = epoch;
-  q.cnt = cnt;
-  const bf16* a = static_cast<const bf16*>(dy);
-  const bf16* b = static_cast<const bf16*>(x);
-  const bf16* c = static_cast<const bf16*>(w);
-  const bf16* d = static_cast<const bf16*>(dres);
-  bf16* o = static_cast<bf16*>(dx);
-  switch (H / 256) {
-    case 1: rmsnorm_bwd_warp_kernel<1, true><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H, q); break;
-    case 2: rmsnorm_bwd_warp_kernel<2, true><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H, q); break;
-    case 4: rmsnorm_bwd_warp_kernel<4, true><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H, q); break;
-    case 8: rmsnorm_bwd_warp_kernel<8, true><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H, q); break;
-    case 16: rmsnorm_bwd_warp_kernel<16, true><<<partial_rows, 256, 0, st>>>(a, b, x_rows, rstd, c, d, o, dw_partial, rows, H, q); break;
-    default: return -11;
   }
   colsum_acc_kernel<<<(H + 31) / 32, 256, 0, st>>>(dw_partial, dw_acc, partial_rows, H);
   return last_err();

@@ -38,25 +38,30 @@ struct GemmArgs {
   const float* cs;
   int rope_cols, hd;
   // ---- tensor-parallel fusion.  Row segments: rank q owns rows [seg[q], seg[q+1]) of A / D
-  // (device array [P + 1]; uniform shards in the forward, kept rows in the backward)
+  // (device array [P + 1]; uniform shards in the forward, kept rows in the backward).  Flags
+  // live in symmetric buffers peer_flags[q]: ready[P] at flag_ready, done[P] at flag_done.
   int rank, P;
   const int* seg;
   uint32_t epoch;
-  // all-gather consumer (TPM 1): A rows of segment q are usable once a_ready[q] >= epoch (local
-  // flags raised by the producer of each segment); m-blocks are rotated by rot_mblocks so the
-  // rank's own segment, ready first, is computed first
-  const uint32_t* a_ready;
-  int rot_mblocks;
-  // reduce-scatter producer (TPM 2): D is this rank's partial-sum buffer (symmetric memory);
-  // flags live in symmetric buffers peer_flags[q] (rs_ready at flag_ready, rs_done at
-  // flag_done, P entries each); tile_cnt is local scratch [P + 2], zero at rest
   uint32_t* const* peer_flags;
   int flag_ready, flag_done;
-  uint32_t* tile_cnt;
-  const __nv_bfloat16* mc_part;            // multicast address of D, or nullptr
-  const __nv_bfloat16* const* peer_part;   // D of every rank (peer loads when no multicast)
-  const __nv_bfloat16* rs_resid;           // [shard rows, N] added to the reduced rows
-  __nv_bfloat16* rs_out;                   // [out_rows, N] reduced rows of this rank, then zeros
+  uint32_t* tile_cnt;  // local scratch [P + 2], zero at rest
+  // all-gather consumer (TPM 1): this rank's rows of A are local; two push warps per CTA copy
+  // them to every other rank (multicast store, or peer stores) and raise ready[rank] there;
+  // the TMA producer waits on ready[q] before reading rows of segment q != rank.  m-blocks are
+  // rotated by rot_mblocks so the local segment is computed first.
+  int rot_mblocks;
+  long long lda;
+  __nv_bfloat16* ag_mc;            // multicast address of A, or nullptr
+  __nv_bfloat16* const* ag_peers;  // A of every rank (peer stores without multicast)
+  // reduce-scatter producer (TPM 2): the epilogue stores each partial row into slot [rank] of
+  // its owner's receive buffer (recv[o] + (rank * seg_cap + local row) * ldd), so partials cross
+  // NVLink while the next tile is computed; two sum warps per CTA add this rank's P slots once
+  // every rank has finished its segment, plus the residual, into rs_out.
+  __nv_bfloat16* const* recv;
+  int seg_cap;
+  const __nv_bfloat16* rs_resid;   // [count, N] added to the reduced rows
+  __nv_bfloat16* rs_out;           // [out_rows, N] reduced rows of this rank, then zeros
   long long ld_resid, ld_out;
   int out_rows;
 };
@@ -91,13 +96,12 @@ __device__ __forceinline__ bool wait_epoch(const uint32_t* flags, int n, uint32_
   }
   return true;
 }
-__device__ __forceinline__ uint4 ld_reduce_bf16x8(const __nv_bfloat16* mc) {
-  uint4 r;
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(mc)
-               : "memory");
-  return r;
+// atomicAdd with acquire-release semantics at GPU scope: publishes this thread's earlier writes
+// (and those it observed) to whoever observes the new count
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 }  // namespace tpc
 
@@ -124,10 +128,10 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   tn = r / gsize;
 }
 
-// TPM: 0 plain; 1 all-gather consumer (A shards waited on per m-block); 2 reduce-scatter
-// producer (partials + per-shard signals + two pull warps that reduce this rank's rows)
+// TPM: 0 plain; 1 all-gather consumer (push warps + per-segment waits); 2 reduce-scatter
+// producer (partial rows stored to their owners + sum warps)
 template <int BN, bool A_MN, bool B_MN, int EPI, int TPM = 0>
-__global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
+__global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
   using S = GemmShape<BN>;
@@ -195,8 +199,12 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
           const int r0 = tm * S::BM, r1 = min(p.M, r0 + S::BM);
           bool waited = false;
           for (int q = 0; q < p.P && ok; ++q) {
-            if (((ready_mask >> q) & 1ull) || p.seg[q] >= r1 || p.seg[q + 1] <= r0) continue;
-            if (!tpc::wait_epoch(p.a_ready + q, 1, p.epoch, abort_flag, p.err)) ok = false;
+            if (q == p.rank || ((ready_mask >> q) & 1ull) || p.seg[q] >= r1 ||
+                p.seg[q + 1] <= r0)
+              continue;
+            if (!tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_ready + q, 1, p.epoch, abort_flag,
+                                 p.err))
+              ok = false;
             ready_mask |= 1ull << q;
             waited = true;
           }
@@ -295,7 +303,7 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
     const int row_in_tile = q * 32 + lane;
     int it = 0;
     if (TPM == 2) {
-      // the partial buffer of this epoch was last read by the pulls of epoch - 2
+      // the receive buffers of this epoch's parity were last read by the sums of epoch - 2
       bool okw = true;
       if (lane == 0)
         okw = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_done, p.P, p.epoch - 2, abort_flag,
@@ -321,6 +329,13 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      // destination of this lane's row: D, or (TPM 2) slot [rank] of the row owner's buffer
+      __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
+      if (TPM == 2 && row < p.M) {
+        int o = 0;
+        while (o < p.P - 1 && row >= p.seg[o + 1]) ++o;
+        drow = p.recv[o] + (static_cast<long long>(p.rank) * p.seg_cap + (row - p.seg[o])) * p.ldd;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col = n0 + c * 32;
@@ -367,7 +382,7 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
           if (EPI == kEpiBF16 || EPI == kEpiBF16Resid || EPI == kEpiBF16Rope) {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+            __nv_bfloat16* dst = drow + col;
             if (EPI == kEpiBF16Resid) {
               const uint4* rs = reinterpret_cast<const uint4*>(p.R + row * p.ldr + col);
 #pragma unroll
@@ -418,12 +433,13 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
         // owner segment it intersects; the last chunk of a segment tells its owner
         const int c0 = m0 + row_in_tile - lane;
         if (c0 < p.M) {
-          __threadfence_system();
           for (int o = 0; o < p.P; ++o) {
             const int lo = p.seg[o], hi = p.seg[o + 1];
             if (hi <= lo || lo >= c0 + 32 || hi <= c0) continue;
             const uint32_t need = static_cast<uint32_t>(((hi + 31) / 32 - lo / 32) * num_n);
-            if (atomicAdd(p.tile_cnt + o, 1u) == need - 1u) {
+            if (tpc::atom_add_acq_rel_gpu(p.tile_cnt + o, 1u) == need - 1u) {
+              // all of the segment's chunks are published at GPU scope: make them visible to
+              // the peers, then raise the owner's flag
               __threadfence_system();
               tpc::st_release_sys(p.peer_flags[o] + p.flag_ready + p.rank, p.epoch);
             }
@@ -431,58 +447,81 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
         }
       }
     }
+  } else if (TPM == 1) {
+    // -------------------------------------------------------------- push warps (6, 7)
+    // Copy this rank's rows of A to every other rank while the tensor cores start on them.
+    const int r_lo = p.seg[p.rank];
+    const int rows = p.seg[p.rank + 1] - r_lo;
+    const int vec_per_row = p.K / 8;
+    const long long total = static_cast<long long>(rows) * vec_per_row;
+    const long long stride = static_cast<long long>(gridDim.x) * 64;
+    const __nv_bfloat16* A = p.ag_peers[p.rank];
+    constexpr int U = 4;
+    for (long long v0 = static_cast<long long>(blockIdx.x) * 64 + (warp - 6) * 32 + lane;
+         v0 < total && !*abort_flag; v0 += U * stride) {
+      uint4 val[U];
+      long long off[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long v = v0 + u * stride;
+        off[u] = -1;
+        if (v < total) {
+          off[u] = static_cast<long long>(r_lo + v / vec_per_row) * p.lda + (v % vec_per_row) * 8;
+          val[u] = *reinterpret_cast<const uint4*>(A + off[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (off[u] < 0) continue;
+        if (p.ag_mc) {
+          asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                           p.ag_mc + off[u]),
+                       "f"(__uint_as_float(val[u].x)), "f"(__uint_as_float(val[u].y)),
+                       "f"(__uint_as_float(val[u].z)), "f"(__uint_as_float(val[u].w))
+                       : "memory");
+        } else {
+          for (int q2 = 0; q2 < p.P; ++q2)
+            if (q2 != p.rank) *reinterpret_cast<uint4*>(p.ag_peers[q2] + off[u]) = val[u];
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      if (tpc::atom_add_acq_rel_gpu(p.tile_cnt, 1u) == 2u * gridDim.x - 1u) {
+        __threadfence_system();
+        for (int q2 = 0; q2 < p.P; ++q2)
+          if (q2 != p.rank) tpc::st_release_sys(p.peer_flags[q2] + p.flag_ready + p.rank, p.epoch);
+      }
+    }
   } else if (TPM == 2) {
-    // -------------------------------------------------------------- pull warps (6, 7)
-    // Rows [rank * shard, (rank + 1) * shard) summed over all ranks' partial buffers (one
-    // multimem.ld_reduce per 8 bf16 through the NVSwitch, fp32 accumulation), plus the
-    // residual, written to rs_out.  Starts as soon as every rank has finished this shard.
+    // -------------------------------------------------------------- sum warps (6, 7)
+    // Once every rank has stored its partials of this rank's segment: rows [0, count) of
+    // out = sum of the P receive slots (local reads) + residual; rows up to out_rows zero.
     bool ok = true;
     if (lane == 0)
       ok = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_ready, p.P, p.epoch, abort_flag, p.err);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     if (ok) {
-      const int r_lo = p.seg[p.rank];
-      const int rows = p.seg[p.rank + 1] - r_lo;  // reduced rows; rows..out_rows-1 are zeroed
+      const int rows = p.seg[p.rank + 1] - p.seg[p.rank];
       const int vec_per_row = p.N / 8;
       const long long total = static_cast<long long>(p.out_rows) * vec_per_row;
-      const int t = (warp - 6) * 32 + lane;
-      for (long long v = static_cast<long long>(blockIdx.x) * 64 + t; v < total;
-           v += static_cast<long long>(gridDim.x) * 64) {
+      const long long stride = static_cast<long long>(gridDim.x) * 64;
+      const __nv_bfloat16* rb = p.recv[p.rank];
+      const long long slot = static_cast<long long>(p.seg_cap) * p.ldd;
+      for (long long v = static_cast<long long>(blockIdx.x) * 64 + (warp - 6) * 32 + lane;
+           v < total; v += stride) {
         const int r = static_cast<int>(v / vec_per_row);
         const int c = static_cast<int>(v % vec_per_row) * 8;
+        uint4* dst = reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c);
         if (r >= rows) {
-          *reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c) =
-              make_uint4(0u, 0u, 0u, 0u);
+          *dst = make_uint4(0u, 0u, 0u, 0u);
           continue;
         }
-        const long long off = static_cast<long long>(r_lo + r) * p.ldd + c;
-        float acc[8];
-        if (p.mc_part) {
-          const uint4 u = tpc::ld_reduce_bf16x8(p.mc_part + off);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            acc[2 * e] = f.x;
-            acc[2 * e + 1] = f.y;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-          for (int q2 = 0; q2 < p.P; ++q2) {
-            const uint4 u = *reinterpret_cast<const uint4*>(p.peer_part[q2] + off);
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = __bfloat1622float2(h[e]);
-              acc[2 * e] += f.x;
-              acc[2 * e + 1] += f.y;
-            }
-          }
-        }
-        if (p.rs_resid) {
-          const uint4 u = *reinterpret_cast<const uint4*>(p.rs_resid + static_cast<long long>(r) * p.ld_resid + c);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const long long off = static_cast<long long>(r) * p.ldd + c;
+        for (int q2 = 0; q2 < p.P; ++q2) {
+          const uint4 w4 = *reinterpret_cast<const uint4*>(rb + q2 * slot + off);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w4);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(h[e]);
@@ -490,15 +529,22 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
             acc[2 * e + 1] += f.y;
           }
         }
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c) = o;
+        if (p.rs_resid) {
+          const uint4 u4 =
+              *reinterpret_cast<const uint4*>(p.rs_resid + static_cast<long long>(r) * p.ld_resid + c);
+          const __nv_bfloat162* hr = reinterpret_cast<const __nv_bfloat162*>(&u4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(hr[e]);
+            acc[2 * e] += f.x;
+            acc[2 * e + 1] += f.y;
+          }
+        }
+        *dst = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
       }
-      // this rank has read its rows of every partial buffer: the last pull warp of the grid
-      // tells all ranks (their buffer of this epoch may be rewritten at epoch + 2)
+      // this rank has read its receive slots: the last sum warp of the grid tells all ranks
+      // (their stores of epoch + 2 may reuse the slots)
       __syncwarp();
       if (lane == 0) {
         __threadfence_system();
@@ -514,7 +560,7 @@ __global__ void __launch_bounds__(TPM == 2 ? 256 : 192, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, S::TMEM_COLS);
-  if (TPM == 2 && threadIdx.x == 0) {
+  if (TPM != 0 && threadIdx.x == 0) {
     // the last CTA to finish clears the local counters for the next launch
     __threadfence();
     if (atomicAdd(p.tile_cnt + p.P + 1, 1u) == gridDim.x - 1u) {
@@ -577,9 +623,9 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
   const int tiles = ((a.M + 127) / 128) * ((a.N + BN - 1) / BN);
   int grid = tiles < num_sms() ? tiles : num_sms();
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-  if (TPM == 2) {
-    // CTAs wait on one another's tiles (through the shard flags): cooperative launch makes
-    // the whole grid co-resident
+  if (TPM != 0) {
+    // CTAs wait on one another's work (through the flags, also across GPUs): cooperative launch
+    // makes the whole grid co-resident
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(256);
@@ -666,30 +712,37 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.rank = 0;
   a.P = 1;
   a.seg = nullptr;
-  a.out_rows = 0;
   a.epoch = 0;
-  a.a_ready = nullptr;
-  a.rot_mblocks = 0;
   a.peer_flags = nullptr;
   a.flag_ready = a.flag_done = 0;
   a.tile_cnt = nullptr;
-  a.mc_part = nullptr;
-  a.peer_part = nullptr;
+  a.rot_mblocks = 0;
+  a.lda = lda;
+  a.ag_mc = nullptr;
+  a.ag_peers = nullptr;
+  a.recv = nullptr;
+  a.seg_cap = 0;
   a.rs_resid = nullptr;
   a.rs_out = nullptr;
   a.ld_resid = a.ld_out = 0;
+  a.out_rows = 0;
   if (tp) {
     if (tp->mode != 1 && tp->mode != 2) return -13;
     if (a_mn) return -13;  // rows of A are the sequence-parallel rows
-    if (tp->P < 1 || tp->P > 64 || !tp->seg || tp->rot_rows % 128) return -13;
+    if (tp->P < 1 || tp->P > 64 || !tp->seg || !tp->peer_flags || !tp->tile_cnt) return -13;
     a.rank = tp->rank;
     a.P = tp->P;
     a.seg = tp->seg;
     a.epoch = tp->epoch;
+    a.peer_flags = tp->peer_flags;
+    a.flag_ready = tp->flag_ready;
+    a.flag_done = tp->flag_done;
+    a.tile_cnt = tp->tile_cnt;
     if (tp->mode == 1) {
-      if (!tp->a_ready) return -13;
-      a.a_ready = tp->a_ready;
+      if (tp->rot_rows % 128 || !tp->ag_peers || (K % 8) || (lda % 8)) return -13;
       a.rot_mblocks = tp->rot_rows / 128;
+      a.ag_mc = static_cast<__nv_bfloat16*>(tp->ag_mc);
+      a.ag_peers = reinterpret_cast<__nv_bfloat16* const*>(tp->ag_peers);
 #define CFB_TP1(BNV, BMN, E) launch_gemm<BNV, false, BMN, E, 1>(ta, tb, a, st, max_ctas)
       if (epi == kEpiBF16) {
         if (b_mn) return bn == 256 ? CFB_TP1(256, true, kEpiBF16) : CFB_TP1(128, true, kEpiBF16);
@@ -700,15 +753,11 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
 #undef CFB_TP1
       return -4;
     }
-    if (epi != kEpiBF16 || !tp->peer_flags || !tp->tile_cnt || !tp->out ||
-        (!tp->mc_part && !tp->peer_part) || (N % 8) || tp->out_rows < 0)
+    if (epi != kEpiBF16 || !tp->recv || !tp->out || (N % 8) || tp->out_rows < 0 ||
+        tp->seg_cap <= 0)
       return -13;
-    a.peer_flags = tp->peer_flags;
-    a.flag_ready = tp->flag_ready;
-    a.flag_done = tp->flag_done;
-    a.tile_cnt = tp->tile_cnt;
-    a.mc_part = static_cast<const __nv_bfloat16*>(tp->mc_part);
-    a.peer_part = reinterpret_cast<const __nv_bfloat16* const*>(tp->peer_part);
+    a.recv = reinterpret_cast<__nv_bfloat16* const*>(tp->recv);
+    a.seg_cap = tp->seg_cap;
     a.rs_resid = static_cast<const __nv_bfloat16*>(tp->resid);
     a.rs_out = static_cast<__nv_bfloat16*>(tp->out);
     a.ld_resid = tp->ld_resid;

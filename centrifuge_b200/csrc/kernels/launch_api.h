@@ -13,29 +13,31 @@ int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long lo
                   void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
                   int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st);
 // Tensor-parallel fusion of a GEMM (A [M, K] K-major; B [N, K] K-major or, with b_mn, [K, N])
-// with a collective over NVLink (gemm_sm100.cu).  The M rows are split into per-rank segments
-// seg[q]..seg[q+1] (device array [P + 1]; uniform sequence-parallel shards in the forward, each
-// rank's kept rows in the filtered backward).
-//   mode 1 (all-gather consumer): A receives every rank's segment (pushed by its producer
-//     through NVSwitch multicast); the GEMM waits on a_ready[q] >= epoch (local flag per source
-//     segment) before reading rows of segment q, starting at row rot_rows (own segment first).
-//   mode 2 (reduce-scatter producer): D is this rank's partial buffer in symmetric memory; each
-//     rank tells a segment's owner when its rows of that segment are stored, and two extra
-//     warps per CTA pull this rank's segment summed over all ranks (multimem.ld_reduce, or peer
-//     loads), add `resid` and write `out` rows [0, count), zeros up to out_rows -- all in the
-//     same (cooperative) launch.
+// with a collective over NVLink (gemm_sm100.cu), in one cooperative launch.  The M rows are
+// split into per-rank segments seg[q]..seg[q+1] (device array [P + 1]; uniform
+// sequence-parallel shards in the forward, each rank's kept rows in the filtered backward).
+// Flags are symmetric buffers peer_flags[q] with ready[P] at flag_ready, done[P] at flag_done.
+//   mode 1 (all-gather into A): this rank's segment of A is already in place; two extra warps
+//     per CTA copy it to every other rank's A (multicast store through the NVSwitch, or peer
+//     stores) and raise ready[rank] there, while the TMA producer reads other segments only
+//     after their ready flag (own segment first).
+//   mode 2 (reduce-scatter of D): the epilogue stores each row's partial sum into slot [rank]
+//     of the row owner's receive buffer (recv[o], rows of seg_cap); two extra warps per CTA
+//     add this rank's P slots once all ranks have signalled, plus `resid`, into `out` rows
+//     [0, count) and zero rows up to out_rows.  D itself is not written.
 struct CfbTpGemm {
   int mode;
   int rank, P;
   const int* seg;                 // device [P + 1]
   uint32_t epoch;
-  const uint32_t* a_ready;        // mode 1: local flags [P]
+  uint32_t* const* peer_flags;    // device array [P] of flag buffers (symmetric memory)
+  int flag_ready, flag_done;
+  uint32_t* tile_cnt;             // local scratch [P + 2], zero at rest
   int rot_rows;                   // mode 1: first row computed (multiple of 128)
-  uint32_t* const* peer_flags;    // mode 2: device array [P] of flag buffers (symmetric)
-  int flag_ready, flag_done;      // mode 2: offsets of rs_ready[P] / rs_done[P] in them
-  uint32_t* tile_cnt;             // mode 2: local scratch [P + 2], zero at rest
-  const void* mc_part;            // mode 2: multicast address of D (or nullptr)
-  const void* const* peer_part;   // mode 2: device array [P] of D pointers (or nullptr)
+  void* ag_mc;                    // mode 1: multicast address of A (or nullptr)
+  void* const* ag_peers;          // mode 1: device array [P] of A on every rank
+  void* const* recv;              // mode 2: device array [P] of receive buffers
+  int seg_cap;                    // mode 2: rows per receive slot
   const void* resid;              // mode 2: [count, N] bf16 (optional)
   long long ld_resid;
   void* out;                      // mode 2: [out_rows, N] bf16
@@ -46,24 +48,6 @@ int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, int 
                 long long ldd, int M, int N, int K, const int* pos, const float* cos_sin,
                 int rope_cols, int head_dim, const CfbTpGemm* tp, int* err, int bn,
                 cudaStream_t st);
-
-// RMSNorm of this rank's rows [rows, H] written into every rank's gather buffer (rows
-// row_base + r) through the multicast address `mc_dst` (or each of `peer_dst[P]`), rstd kept
-// locally; then ready[rank] = epoch is raised at flag_off in every rank's flag buffer
-// (tp_comm_sm100.cu).  `cnt` is a local zero-at-rest counter.
-int cfb_tp_rmsnorm_push(const void* x, const void* w, int rows, int H, float eps, void* mc_dst,
-                        void* const* peer_dst, long long ld_dst, float* rstd,
-                        uint32_t* const* peer_flags, int flag_off, int rank, int P,
-                        int row_base, uint32_t epoch, uint32_t* cnt, cudaStream_t st);
-// RMSNorm backward (as cfb_rmsnorm_bwd) whose output rows [0, count) are also written into
-// every rank's gather buffer at rows row_base + r, followed by ready[rank] = epoch on every rank
-// (fused_ops.cu).  H must be a multiple of 256 (<= 4096).
-int cfb_tp_rmsnorm_bwd_push(const void* dy, const void* x, const int* x_rows, const float* rstd,
-                            const void* w, const void* dres, void* dx, float* dw_partial,
-                            float* dw_acc, int rows, int H, int partial_rows, void* mc_dst,
-                            void* const* peer_dst, long long ld_dst, int row_base, int count,
-                            uint32_t* const* peer_flags, int flag_off, int rank, int P,
-                            uint32_t epoch, uint32_t* cnt, cudaStream_t st);
 
 // Forward projection with rotate-half RoPE fused into the epilogue: D = A B^T (both K-major) and
 // columns [0, rope_cols) rotated per head of head_dim (64 or 128) at position pos[row], using the

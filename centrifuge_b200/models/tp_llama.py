@@ -222,13 +222,13 @@ class TPLlamaCore(torch.nn.Module):
         for li, i in enumerate(self.layer_ids):
             pre = f"layers.{i}."
             L = {"x": x}
-            xn, r1, e1 = comm.rmsnorm_push(x, p[pre + "ln1"], eps, 2 * li)
-            qkv = comm.gemm_ag(xn, p[pre + "wqkv"], e1,
+            xn, r1 = comm.rmsnorm_local(x, p[pre + "ln1"], eps, 2 * li)
+            qkv = comm.gemm_ag(xn, p[pre + "wqkv"], 2 * li,
                                rope=(pos, self._rope, (nh + nkv) * hd, hd))
             o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd, scale=self.scale)
             x2 = comm.gemm_rs(o, p[pre + "wo"], x)
-            xn2, r2, e2 = comm.rmsnorm_push(x2, p[pre + "ln2"], eps, 2 * li + 1)
-            gu = comm.gemm_ag(xn2, p[pre + "wgu"], e2)
+            xn2, r2 = comm.rmsnorm_local(x2, p[pre + "ln2"], eps, 2 * li + 1)
+            gu = comm.gemm_ag(xn2, p[pre + "wgu"], 2 * li + 1)
             h = fused.swiglu_fwd(gu)
             x = comm.gemm_rs(h, p[pre + "wd"], x2)
             L.update(xn=xn, rstd1=r1, qkv=qkv, o=o, lse=lse, x2=x2, xn2=xn2, rstd2=r2, gu=gu, h=h)
@@ -236,8 +236,9 @@ class TPLlamaCore(torch.nn.Module):
         sv["fused"] = True
         if not self.has_head:
             return x, sv
-        xf, rf, ef = comm.rmsnorm_push(x, p["norm"], eps, 2 * len(self.layer_ids))
-        logits = comm.gemm_ag(xf, p["lm_head"], ef)
+        fslot = 2 * len(self.layer_ids)
+        xf, rf = comm.rmsnorm_local(x, p["norm"], eps, fslot)
+        logits = comm.gemm_ag(xf, p["lm_head"], fslot)
         return self._head_loss(logits, x, xf, rf, input_ids, labels, B, S, sv)
 
     # ------------------------------------------------------------------ backward
@@ -365,14 +366,14 @@ def _backward_fused_impl(self, sv, grad_out, state, lay, rows, Sk, pos_flat, pos
     dxf_p = comm.gemm_rs(dlogits, p["lm_head"], None, seg=seg, b_mn=True, out_rows=C)
     del dlogits, xf_k
     layers = list(enumerate(self.layer_ids))
-    # dx of the final norm, gathered for the last layer's down projection
-    dx, dYg, ea = comm.rmsnorm_bwd_push(dxf_p, hd_["x"], hd_["rstdf"], p["norm"], g["norm"],
-                                        local, None, slot_a, seg)
+    # dx of the final norm; its kept rows are all-gathered by the last layer's down dgrad
+    dx = fused.rmsnorm_bwd(dxf_p, hd_["x"], hd_["rstdf"], p["norm"], g["norm"], x_rows=local)
+    dYg = comm.place_rows(dx, slot_a, seg)
     for li, i in reversed(layers):
         L = sv["layers"][li]
         pre = f"layers.{i}."
-        # ---- MLP: dgrad first (it waits for the gathered rows), then wgrad
-        dh = comm.gemm_ag(dYg, p[pre + "wd"], ea, seg=seg, b_mn=True)
+        # ---- MLP: dgrad first (it gathers the rows), then wgrad reads the gathered rows
+        dh = comm.gemm_ag(dYg, p[pre + "wd"], slot_a, seg=seg, b_mn=True)
         h_k = gat(L["h"])
         G.linear_wgrad(dYg, h_k, g[pre + "wd"])
         del h_k
@@ -382,11 +383,12 @@ def _backward_fused_impl(self, sv, grad_out, state, lay, rows, Sk, pos_flat, pos
         G.linear_wgrad(dgu, xn2_k, g[pre + "wgu"])
         dxn2_p = comm.gemm_rs(dgu, p[pre + "wgu"], None, seg=seg, b_mn=True, out_rows=C)
         del dgu, xn2_k
-        dx2, dY2g, eb = comm.rmsnorm_bwd_push(dxn2_p, L["x2"], L["rstd2"], p[pre + "ln2"],
-                                              g[pre + "ln2"], local, dx, slot_b, seg)
+        dx2 = fused.rmsnorm_bwd(dxn2_p, L["x2"], L["rstd2"], p[pre + "ln2"], g[pre + "ln2"],
+                                x_rows=local, dres=dx)
+        dY2g = comm.place_rows(dx2, slot_b, seg)
         del dxn2_p, dx
         # ---- attention
-        do = comm.gemm_ag(dY2g, p[pre + "wo"], eb, seg=seg, b_mn=True)
+        do = comm.gemm_ag(dY2g, p[pre + "wo"], slot_b, seg=seg, b_mn=True)
         o_k = gat(L["o"])
         G.linear_wgrad(dY2g, o_k, g[pre + "wo"])
         qkv_k = gat(L["qkv"])
@@ -399,12 +401,10 @@ def _backward_fused_impl(self, sv, grad_out, state, lay, rows, Sk, pos_flat, pos
         G.linear_wgrad(dqkv, xn_k, g[pre + "wqkv"])
         dxn_p = comm.gemm_rs(dqkv, p[pre + "wqkv"], None, seg=seg, b_mn=True, out_rows=C)
         del dqkv, xn_k
+        dx = fused.rmsnorm_bwd(dxn_p, L["x"], L["rstd1"], p[pre + "ln1"], g[pre + "ln1"],
+                               x_rows=local, dres=dx2)
         if li > 0:
-            dx, dYg, ea = comm.rmsnorm_bwd_push(dxn_p, L["x"], L["rstd1"], p[pre + "ln1"],
-                                                g[pre + "ln1"], local, dx2, slot_a, seg)
-        else:
-            dx = fused.rmsnorm_bwd(dxn_p, L["x"], L["rstd1"], p[pre + "ln1"], g[pre + "ln1"],
-                                   x_rows=local, dres=dx2)
+            dYg = comm.place_rows(dx, slot_a, seg)
         del dxn_p, dx2
         sv["layers"][li] = None
     if self.has_embed:

@@ -13,7 +13,7 @@ _err = None
 _proxy = None
 
 # Kernels launched by one call of each binding (for the launch counter).
-_LAUNCHES_PER_CALL = {"rmsnorm_bwd": 2, "tp_rmsnorm_bwd_push": 2, "attn_bwd": 2, "attn_bwd_mma": 3, "gemm_error_word": 0}
+_LAUNCHES_PER_CALL = {"rmsnorm_bwd": 2, "attn_bwd": 2, "attn_bwd_mma": 3, "gemm_error_word": 0}
 
 
 class LaunchCounter:

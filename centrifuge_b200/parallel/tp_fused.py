@@ -2,27 +2,29 @@
 
 Sequence-parallel Megatron layers move activations with an all-gather before every
 column-parallel GEMM and a reduce-scatter after every row-parallel GEMM (reference:
-model/megatronlm.py:64-99, 152-178; those run as separate NCCL kernels).  Here both are fused
-into the kernels that produce or consume the data:
+model/megatronlm.py:64-99, 152-178; those run as separate NCCL kernels).  Here both happen
+inside the GEMM kernel (``gemm_tp``, csrc/kernels/gemm_sm100.cu), in one cooperative launch:
 
-* all-gather: the RMSNorm kernel of the rank's rows writes its output once into every rank's
-  gather buffer through the NVSwitch multicast address (or peer stores without multicast) and
-  raises per-shard ready flags; the column-parallel GEMM waits on each shard's flag inside its
-  TMA producer and starts with its own shard (``gemm_tp`` mode 1, optionally with the RoPE
-  epilogue), so the transfer of remote shards overlaps its math;
-* reduce-scatter: the row-parallel GEMM writes partial sums into this rank's symmetric partial
-  buffer and tells each shard's owner when that shard's tiles are stored; two extra warps per CTA
-  of the same cooperative launch wait for the rank's own shard and pull it summed over all ranks
-  (``multimem.ld_reduce`` with fp32 accumulation through the switch, or peer loads), add the
-  residual and write the layer output (``gemm_tp`` mode 2).
+* all-gather (mode 1): the producer (RMSNorm forward or backward) writes the rank's rows into
+  its own copy of a symmetric gather buffer; two extra warps per CTA of the consuming GEMM copy
+  them to every other rank (one multicast store per 16 bytes through the NVSwitch, or peer
+  stores) and raise a ready flag there, while the tensor cores start on the local rows (the m
+  blocks are rotated so the own segment comes first); the TMA producer reads another rank's
+  rows only after its flag;
+* reduce-scatter (mode 2): the epilogue stores each partial row straight into slot [rank] of
+  the row owner's receive buffer over NVLink (overlapping the next tile's MMAs) and counts rows
+  per owner; when an owner's segment is complete everywhere, two extra warps per CTA of the
+  owner add its P slots (local reads) and the residual into the layer output.
 
-Buffers live in ``torch.distributed._symmetric_memory`` (same offsets on every rank).  The
-gather buffers are per call site ("slots", e.g. two per layer) and double as the saved
-activations of the backward, so a slot is rewritten only by the next micro-batch's forward.  The
-two partial buffers alternate by epoch; a GEMM of epoch e waits until every rank finished
-pulling from epoch e - 2.  Flags carry monotonically increasing epochs (never reset); every rank
-issues the same sequence of fused calls, so epochs agree across the group.  All waits are
-bounded (20 s) and report through the kernels' error word.
+Rows are split into per-rank segments (:class:`Segments`): uniform sequence-parallel shards in
+the forward, each rank's kept rows (compact global order) in the filtered backward, so the
+GEMMs see exactly the kept rows.  Buffers live in ``torch.distributed._symmetric_memory``.  The
+gather buffers are per call site ("slots", two per layer) and double as the saved activations
+of the backward, so a slot is rewritten only by the next micro-batch's forward; the receive
+buffers alternate by epoch and a GEMM of epoch e waits until every rank finished reading epoch
+e - 2.  Flags carry monotonically increasing epochs (never reset); every rank issues the same
+sequence of fused calls, so epochs agree across the group.  All waits are bounded (20 s) and
+report through the kernels' error word.
 """
 from __future__ import annotations
 
@@ -30,6 +32,7 @@ from typing import Optional, Tuple
 
 import torch
 
+from ..ops import fused
 from ..ops._ext import kernels
 
 
@@ -53,7 +56,7 @@ class TPFusedComm:
         self.flags.zero_()
         self.fhdl = symm_mem.rendezvous(self.flags, tp.group)
         self.peer_flags_dev = int(self.fhdl.buffer_ptrs_dev)
-        self.ag_ready = self.flags.data_ptr()  # local ready[P] of the gathers (offset 0)
+        # flag layout: gather ready[P] at 0, reduce-scatter ready[P] at P, done[P] at 2P
         self.off_rs_ready, self.off_rs_done = P, 2 * P
         mc_ok = use_multicast and self.ghdl.has_multicast_support and self.phdl.has_multicast_support
         self.g_mc = int(self.ghdl.multicast_ptr) if mc_ok else 0
@@ -67,7 +70,6 @@ class TPFusedComm:
         self.p_peers = [torch.tensor([b + i * T * H * esz for b in pb], dtype=torch.int64,
                                      device=self.device) for i in range(2)]
         self.cnt = torch.zeros(P + 2, dtype=torch.int32, device=self.device)
-        self.push_cnt = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ag_epoch = 0
         self.rs_epoch = 0
         self._uniform = None
@@ -92,58 +94,51 @@ class TPFusedComm:
     def _mc(self, base: int, slot_elems: int) -> int:
         return base + slot_elems * 2 if base else 0
 
-    # ---------------------------------------------------------------- all-gather producers
-    def rmsnorm_push(self, x_local: torch.Tensor, w: torch.Tensor, eps: float,
-                     slot: int) -> Tuple[torch.Tensor, torch.Tensor, int]:
-        """RMSNorm of the local shard (uniform segments), gathered into slot ``slot``.
+    # ---------------------------------------------------------------- all-gather
+    def rmsnorm_local(self, x_local: torch.Tensor, w: torch.Tensor, eps: float,
+                      slot: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """RMSNorm of this rank's shard written into its rows of gather slot ``slot``.
 
-        Returns ``(gathered [T, H] view, rstd [shard], epoch)``; the gathered rows are complete
-        only for a consumer that waits on ``epoch`` (:meth:`gemm_ag`)."""
-        assert x_local.shape[0] == self.shard and x_local.shape[1] == self.H
-        self.ag_epoch += 1
-        rstd = torch.empty(self.shard, dtype=torch.float32, device=self.device)
-        T, H = self.T, self.H
-        kernels().tp_rmsnorm_push(x_local, w, eps, self._mc(self.g_mc, slot * T * H),
-                                  self.g_peers[slot].data_ptr(), H, rstd, self.peer_flags_dev, 0,
-                                  self.rank, self.P, self.rank * self.shard, self.ag_epoch,
-                                  self.push_cnt)
-        return self.gather_view(slot), rstd, self.ag_epoch
+        Returns ``(slot [T, H] view, rstd [shard])``; the other ranks' rows arrive during the
+        consuming :meth:`gemm_ag`."""
+        seg = self.uniform_segments()
+        xg = self.gather_view(slot)
+        r0 = seg.start[self.rank]
+        _, rstd = fused.rmsnorm_fwd(x_local, w, eps, out=xg[r0:r0 + self.shard])
+        return xg, rstd
 
-    def rmsnorm_bwd_push(self, dy, x, rstd, w, dw_acc, x_rows, dres, slot: int,
-                         seg: "Segments") -> Tuple[torch.Tensor, torch.Tensor, int]:
-        """RMSNorm backward of the local (padded) rows whose first ``count`` output rows are also
-        gathered into slot ``slot`` at this rank's segment.  Returns ``(dx [rows, H],
-        gathered [Tk, H] view, epoch)``."""
-        self.ag_epoch += 1
-        T, H = self.T, self.H
-        dx = torch.empty_like(dy)
-        partial_rows = max(1, min(dy.shape[0], 148 * 2))
-        kernels().tp_rmsnorm_bwd_push(dy, x, x_rows, rstd, w, dres, dx, dw_acc, partial_rows,
-                                      self._mc(self.g_mc, slot * T * H),
-                                      self.g_peers[slot].data_ptr(), H, seg.start[self.rank],
-                                      seg.counts[self.rank], self.peer_flags_dev, 0, self.rank,
-                                      self.P, self.ag_epoch, self.push_cnt)
-        return dx, self.gather_view(slot, seg.total), self.ag_epoch
+    def place_rows(self, rows_local: torch.Tensor, slot: int, seg: "Segments") -> torch.Tensor:
+        """Write this rank's segment (first ``count`` local rows) into slot ``slot``; returns
+        the slot view of the ``seg.total`` gathered rows."""
+        xg = self.gather_view(slot, seg.total)
+        r0, n = seg.start[self.rank], seg.counts[self.rank]
+        if n:
+            xg[r0:r0 + n].copy_(rows_local[:n])
+        return xg
 
-    # ---------------------------------------------------------------- consumers / producers
-    def gemm_ag(self, xg: torch.Tensor, w: torch.Tensor, epoch: int,
+    def gemm_ag(self, xg: torch.Tensor, w: torch.Tensor, slot: int,
                 rope: Optional[Tuple[torch.Tensor, torch.Tensor, int, int]] = None,
                 seg: Optional["Segments"] = None, b_mn: bool = False,
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """``xg @ w^T`` (``xg @ w`` with ``b_mn``) where ``xg`` is a gathered slot, waiting per
-        source segment inside the kernel."""
+        """``xg @ w^T`` (``xg @ w`` with ``b_mn``) for a gather slot whose own rows are in place:
+        the kernel all-gathers the other segments while it computes."""
         seg = seg or self.uniform_segments()
         N = w.shape[1] if b_mn else w.shape[0]
         if out is None:
             out = torch.empty(xg.shape[0], N, dtype=xg.dtype, device=self.device)
+        self.ag_epoch += 1
         if xg.shape[0] == 0:
             return out
         pos, table, rc, hd = rope if rope is not None else (None, None, 0, 0)
         rot = (seg.start[self.rank] // 128) * 128
+        T, H = self.T, self.H
         kernels().gemm_tp(xg, w, out, b_mn, pos, table, rc, hd, 1, self.rank, self.P, seg.dev,
-                          epoch, self.ag_ready, rot, 0, 0, 0, None, 0, 0, None, None)
+                          self.ag_epoch, self.peer_flags_dev, 0, 0, self.cnt, rot,
+                          self._mc(self.g_mc, slot * T * H), self.g_peers[slot].data_ptr(), 0, 0,
+                          None, None)
         return out
 
+    # ---------------------------------------------------------------- reduce-scatter
     def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, resid: Optional[torch.Tensor],
                 seg: Optional["Segments"] = None, b_mn: bool = False,
                 out_rows: Optional[int] = None, out: Optional[torch.Tensor] = None
@@ -154,17 +149,20 @@ class TPFusedComm:
         T = a.shape[0]
         N = w.shape[1] if b_mn else w.shape[0]
         assert T == seg.total and T <= self.T and N <= self.H
+        assert max(seg.counts) <= self.shard
         self.rs_epoch += 1
         e = self.rs_epoch
         i = e & 1
-        part = self.pbuf[i * self.T * self.H:i * self.T * self.H + max(T, 1) * N].view(-1, N)[:T]
+        carrier = self.pbuf[i * self.T * self.H:i * self.T * self.H + max(T, 1) * N].view(-1, N)[:T]
         rows = seg.counts[self.rank] if out_rows is None else out_rows
         if out is None:
             out = torch.empty(rows, N, dtype=a.dtype, device=self.device)
-        kernels().gemm_tp(a, w, part, b_mn, None, None, 0, 0, 2, self.rank, self.P, seg.dev, e, 0,
-                          0, self.peer_flags_dev, self.off_rs_ready, self.off_rs_done, self.cnt,
-                          self._mc(self.p_mc, i * self.T * self.H), self.p_peers[i].data_ptr(),
-                          resid, out)
+        if T == 0:
+            out.zero_()
+            return out
+        kernels().gemm_tp(a, w, carrier, b_mn, None, None, 0, 0, 2, self.rank, self.P, seg.dev,
+                          e, self.peer_flags_dev, self.off_rs_ready, self.off_rs_done, self.cnt,
+                          0, 0, 0, self.p_peers[i].data_ptr(), self.shard, resid, out)
         return out
 
 
