@@ -47,6 +47,7 @@ def main():
     T, H, nh, nkv, hd, F = a.tokens, 4096, 32, 8, 128, 14336
     tp = TPGroup(dist.group.WORLD)
     comm = TPFusedComm(tp, T, H, 4, dev)
+    comm_p2p = TPFusedComm(tp, T, H, 4, dev, use_multicast=False)
     shard = T // P
     g = torch.Generator(device=dev).manual_seed(rank)
     bf = torch.bfloat16
@@ -73,32 +74,37 @@ def main():
             return G.linear_fwd_rope(xg, w, pos, table, rc, hd)
         return G.linear_fwd(xg, w)
 
-    def fused_ag(w, rope, slot):
-        xg, _ = comm.rmsnorm_local(x, ln, 1e-5, slot)
-        return comm.gemm_ag(xg, w, slot, rope=(pos, table, rc, hd) if rope else None)
+    def fused_ag(w, rope, slot, c=comm):
+        xg, _ = c.rmsnorm_local(x, ln, 1e-5, slot)
+        return c.gemm_ag(xg, w, slot, rope=(pos, table, rc, hd) if rope else None)
 
     def nccl_rs(a_, w):
         return tp.reduce_scatter_rows(G.linear_fwd(a_, w)) + x
 
-    def fused_rs(a_, w):
-        return comm.gemm_rs(a_, w, x)
+    def fused_rs(a_, w, c=comm):
+        return c.gemm_rs(a_, w, x)
 
+    cp = comm_p2p
     ops = {
         "ag_qkv": (lambda: nccl_ag(wqkv, True), lambda: fused_ag(wqkv, True, 0),
+                   lambda: fused_ag(wqkv, True, 0, cp),
                    2.0 * T * H * wqkv.shape[0], (P - 1) / P * T * H * 2),
         "ag_gu": (lambda: nccl_ag(wgu, False), lambda: fused_ag(wgu, False, 1),
+                  lambda: fused_ag(wgu, False, 1, cp),
                   2.0 * T * H * wgu.shape[0], (P - 1) / P * T * H * 2),
-        "rs_o": (lambda: nccl_rs(o, wo), lambda: fused_rs(o, wo),
+        "rs_o": (lambda: nccl_rs(o, wo), lambda: fused_rs(o, wo), lambda: fused_rs(o, wo, cp),
                  2.0 * T * wo.shape[1] * H, (P - 1) / P * T * H * 2),
-        "rs_down": (lambda: nccl_rs(h, wd), lambda: fused_rs(h, wd),
+        "rs_down": (lambda: nccl_rs(h, wd), lambda: fused_rs(h, wd), lambda: fused_rs(h, wd, cp),
                     2.0 * T * wd.shape[1] * H, (P - 1) / P * T * H * 2),
     }
     # correctness spot check of the fused ops against NCCL
-    for name, (fn_n, fn_f, _, _) in ops.items():
-        ref, got = fn_n(), fn_f()
-        err = float((got.float() - ref.float()).norm() / (ref.float().norm() + 1e-12))
-        if err > 2e-2 and rank == 0:
-            print(f"warning: {name} fused vs nccl rel err {err:.3g}", flush=True)
+    for name, (fn_n, fn_f, fn_p, _, _) in ops.items():
+        ref = fn_n()
+        for tag, fn in (("multicast", fn_f), ("p2p", fn_p)):
+            got = fn()
+            err = float((got.float() - ref.float()).norm() / (ref.float().norm() + 1e-12))
+            if err > 2e-2 and rank == 0:
+                print(f"warning: {name} fused ({tag}) vs nccl rel err {err:.3g}", flush=True)
 
     def time_it(fn):
         for _ in range(a.warmup):
@@ -116,12 +122,13 @@ def main():
         return float(t)
 
     res = {}
-    for name, (fn_n, fn_f, flops, link_bytes) in ops.items():
-        tn, tf = time_it(fn_n), time_it(fn_f)
+    for name, (fn_n, fn_f, fn_p, flops, link_bytes) in ops.items():
+        tn, tf, tp2 = time_it(fn_n), time_it(fn_f), time_it(fn_p)
         roof_ms = max(flops / (PEAK_TFLOPS * 1e12), link_bytes / (LINK_GBS * 1e9)) * 1e3
-        res[name] = dict(nccl_ms=tn, fused_ms=tf, roofline_ms=roof_ms,
-                         fused_of_roofline=roof_ms / tf, nccl_of_roofline=roof_ms / tn,
-                         gemm_tflop=flops / 1e12, link_mb=link_bytes / 1e6)
+        res[name] = dict(nccl_ms=tn, fused_multicast_ms=tf, fused_p2p_ms=tp2,
+                         roofline_ms=roof_ms, fused_of_roofline=roof_ms / min(tf, tp2),
+                         nccl_of_roofline=roof_ms / tn, gemm_tflop=flops / 1e12,
+                         link_mb=link_bytes / 1e6)
     if rank == 0:
         print(json.dumps({"P": P, "tokens": T, "comm": comm.kind, "ops": res}, indent=1),
               flush=True)

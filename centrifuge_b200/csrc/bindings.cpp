@@ -122,17 +122,17 @@ void gemm_rope(const Tensor& a, const Tensor& b, Tensor& out, const Tensor& pos,
 
 // ---- tensor-parallel fusion (pointers into symmetric memory are raw device addresses)
 // out = a @ b^T (a @ b with b_mn) fused with a sequence-parallel collective over NVLink:
-// mode 1 all-gathers this rank's rows of `a` to every rank while computing, mode 2 stores the
-// partial rows into their owners' receive buffers and writes this rank's reduced rows (+resid)
-// into `rs_out` (`out` is then only a shape carrier and is not written).
+// mode 1 all-gathers this rank's rows of `a` to every rank while computing, mode 2 writes the
+// partials into `out` (this rank's symmetric partial buffer) and this rank's reduced rows
+// (+resid) into `rs_out`.
 void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
              const c10::optional<Tensor>& pos, const c10::optional<Tensor>& table,
              int64_t rope_cols, int64_t hd, int64_t mode, int64_t rank, int64_t P,
              const Tensor& seg, int64_t epoch, int64_t peer_flags_dev, int64_t flag_ready,
              int64_t flag_done, Tensor& tile_cnt, int64_t rot_rows, int64_t ag_mc,
-             int64_t ag_peers_dev, int64_t recv_dev, int64_t seg_cap,
-             const c10::optional<Tensor>& resid, const c10::optional<Tensor>& rs_out,
-             int64_t bn) {
+             int64_t ag_peers_dev, int64_t mc_part, int64_t peer_part_dev, int64_t flag_blk,
+             int64_t interleave_spb, const c10::optional<Tensor>& resid,
+             const c10::optional<Tensor>& rs_out, int64_t bn) {
   check_bf16_2d(a, "a");
   check_bf16_2d(b, "b");
   check_bf16_2d(out, "out");
@@ -141,7 +141,9 @@ void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
               "gemm_tp: shapes");
   TORCH_CHECK(seg.is_cuda() && seg.scalar_type() == at::kInt && seg.numel() == P + 1,
               "gemm_tp: seg must be int32 [P + 1] on the device");
-  TORCH_CHECK(tile_cnt.scalar_type() == at::kInt && tile_cnt.numel() >= P + 2, "tile_cnt");
+  TORCH_CHECK(tile_cnt.scalar_type() == at::kInt &&
+                  tile_cnt.numel() >= std::max<int64_t>(P, (M + 127) / 128) + 2,
+              "tile_cnt");
   CfbTpGemm t = {};
   t.mode = static_cast<int>(mode);
   t.rank = static_cast<int>(rank);
@@ -155,8 +157,10 @@ void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
   t.rot_rows = static_cast<int>(rot_rows);
   t.ag_mc = reinterpret_cast<void*>(ag_mc);
   t.ag_peers = reinterpret_cast<void* const*>(ag_peers_dev);
-  t.recv = reinterpret_cast<void* const*>(recv_dev);
-  t.seg_cap = static_cast<int>(seg_cap);
+  t.mc_part = reinterpret_cast<const void*>(mc_part);
+  t.peer_part = reinterpret_cast<const void* const*>(peer_part_dev);
+  t.flag_blk = static_cast<int>(flag_blk);
+  t.interleave_spb = static_cast<int>(interleave_spb);
   if (resid.has_value() && resid->defined()) {
     check_bf16_2d(*resid, "resid");
     t.resid = resid->data_ptr();
@@ -584,7 +588,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rank"), py::arg("P"), py::arg("seg"), py::arg("epoch"),
         py::arg("peer_flags_dev"), py::arg("flag_ready"), py::arg("flag_done"),
         py::arg("tile_cnt"), py::arg("rot_rows"), py::arg("ag_mc"), py::arg("ag_peers_dev"),
-        py::arg("recv_dev"), py::arg("seg_cap"), py::arg("resid"), py::arg("rs_out"),
+        py::arg("mc_part"), py::arg("peer_part_dev"), py::arg("flag_blk"),
+        py::arg("interleave_spb"), py::arg("resid"), py::arg("rs_out"),
         py::arg("bn") = 0);
   m.def("gemm_rope", &gemm_rope, "tcgen05 bf16 GEMM with RoPE fused into the epilogue",
         py::arg("a"), py::arg("b"), py::arg("out"), py::arg("pos"), py::arg("table"),

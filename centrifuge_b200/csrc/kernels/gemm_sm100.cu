@@ -54,12 +54,16 @@ struct GemmArgs {
   long long lda;
   __nv_bfloat16* ag_mc;            // multicast address of A, or nullptr
   __nv_bfloat16* const* ag_peers;  // A of every rank (peer stores without multicast)
-  // reduce-scatter producer (TPM 2): the epilogue stores each partial row into slot [rank] of
-  // its owner's receive buffer (recv[o] + (rank * seg_cap + local row) * ldd), so partials cross
-  // NVLink while the next tile is computed; two sum warps per CTA add this rank's P slots once
-  // every rank has finished its segment, plus the residual, into rs_out.
-  __nv_bfloat16* const* recv;
-  int seg_cap;
+  // reduce-scatter producer (TPM 2): D is this rank's partial buffer (symmetric memory).  When
+  // all of an m-block's tiles are stored, the rank raises blk_ready[m][rank] (at flag_blk +
+  // m * P + rank) at every owner of a row of that block; two pull warps per CTA of the owner
+  // reduce its segment block by block as soon as every rank has stored the block (one
+  // multimem.ld_reduce per 8 bf16 through the NVSwitch, fp32 accumulation, or peer loads).
+  // With uniform segments of interleave_spb m-blocks the m-blocks are computed interleaved
+  // across owners, so every owner's blocks complete (and are pulled) during the GEMM.
+  const __nv_bfloat16* mc_part;
+  const __nv_bfloat16* const* peer_part;
+  int flag_blk, interleave_spb;
   const __nv_bfloat16* rs_resid;   // [count, N] added to the reduced rows
   __nv_bfloat16* rs_out;           // [out_rows, N] reduced rows of this rank, then zeros
   long long ld_resid, ld_out;
@@ -68,6 +72,14 @@ struct GemmArgs {
 
 namespace tpc {
 constexpr uint64_t kPeerWaitNs = 20000000000ull;  // 20 s
+__device__ __forceinline__ uint4 ld_reduce_bf16x8(const __nv_bfloat16* mc) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc)
+               : "memory");
+  return r;
+}
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* f) {
   uint32_t v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
@@ -193,6 +205,7 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int tm, tn;
         tile_coords(tile, num_m, num_n, tm, tn);
+        if (TPM == 2 && p.interleave_spb > 0) tm = (tm % p.P) * p.interleave_spb + tm / p.P;
         if (TPM == 1) {
           tm = (tm + p.rot_mblocks) % num_m;
           // wait for every segment that intersects this m-block
@@ -303,23 +316,18 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
     const int row_in_tile = q * 32 + lane;
     int it = 0;
     if (TPM == 2) {
-      // the receive buffers of this epoch's parity were last read by the sums of epoch - 2
+      // the partial buffer of this epoch's parity was last read by the pulls of epoch - 2
       bool okw = true;
       if (lane == 0)
         okw = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_done, p.P, p.epoch - 2, abort_flag,
                               p.err);
       (void)__shfl_sync(0xffffffffu, okw ? 1 : 0, 0);  // on timeout abort_flag is raised
-      if (blockIdx.x == 0 && warp == 2 && lane == 0 && okw) {
-        // owners of empty segments receive nothing from this rank: tell them at once
-        for (int o = 0; o < p.P; ++o)
-          if (p.seg[o + 1] <= p.seg[o])
-            tpc::st_release_sys(p.peer_flags[o] + p.flag_ready + p.rank, p.epoch);
-      }
     }
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       if (TPM == 2 && *abort_flag) break;
       int tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
+      if (TPM == 2 && p.interleave_spb > 0) tm = (tm % p.P) * p.interleave_spb + tm / p.P;
       if (TPM == 1) tm = (tm + p.rot_mblocks) % num_m;
       const int m0 = tm * S::BM, n0 = tn * BN;
       const int acc = it & 1;
@@ -329,13 +337,7 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      // destination of this lane's row: D, or (TPM 2) slot [rank] of the row owner's buffer
       __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
-      if (TPM == 2 && row < p.M) {
-        int o = 0;
-        while (o < p.P - 1 && row >= p.seg[o + 1]) ++o;
-        drow = p.recv[o] + (static_cast<long long>(p.rank) * p.seg_cap + (row - p.seg[o])) * p.ldd;
-      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col = n0 + c * 32;
@@ -429,21 +431,14 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
       if (TPM == 2 && lane == 0) {
-        // this warp stored rows [c0, c0 + 32) of the tile: count the 32-row chunk for every
-        // owner segment it intersects; the last chunk of a segment tells its owner
-        const int c0 = m0 + row_in_tile - lane;
-        if (c0 < p.M) {
-          for (int o = 0; o < p.P; ++o) {
-            const int lo = p.seg[o], hi = p.seg[o + 1];
-            if (hi <= lo || lo >= c0 + 32 || hi <= c0) continue;
-            const uint32_t need = static_cast<uint32_t>(((hi + 31) / 32 - lo / 32) * num_n);
-            if (tpc::atom_add_acq_rel_gpu(p.tile_cnt + o, 1u) == need - 1u) {
-              // all of the segment's chunks are published at GPU scope: make them visible to
-              // the peers, then raise the owner's flag
-              __threadfence_system();
-              tpc::st_release_sys(p.peer_flags[o] + p.flag_ready + p.rank, p.epoch);
-            }
-          }
+        // count this warp's quarter of the tile; the last of the m-block's 4 * num_n quarters
+        // tells every owner of a row of the block
+        if (tpc::atom_add_acq_rel_gpu(p.tile_cnt + tm, 1u) == 4u * num_n - 1u) {
+          __threadfence_system();
+          const int r1 = min(p.M, m0 + S::BM);
+          for (int o = 0; o < p.P; ++o)
+            if (p.seg[o] < r1 && p.seg[o + 1] > m0)
+              tpc::st_release_sys(p.peer_flags[o] + p.flag_blk + tm * p.P + p.rank, p.epoch);
         }
       }
     }
@@ -494,61 +489,93 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       }
     }
   } else if (TPM == 2) {
-    // -------------------------------------------------------------- sum warps (6, 7)
-    // Once every rank has stored its partials of this rank's segment: rows [0, count) of
-    // out = sum of the P receive slots (local reads) + residual; rows up to out_rows zero.
+    // -------------------------------------------------------------- pull warps (6, 7)
+    const int lo = p.seg[p.rank], hi = p.seg[p.rank + 1];
+    const int vec_per_row = p.N / 8;
+    const long long stride = static_cast<long long>(gridDim.x) * 64;
+    const long long t0 = static_cast<long long>(blockIdx.x) * 64 + (warp - 6) * 32 + lane;
     bool ok = true;
-    if (lane == 0)
-      ok = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_ready, p.P, p.epoch, abort_flag, p.err);
-    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-    if (ok) {
-      const int rows = p.seg[p.rank + 1] - p.seg[p.rank];
-      const int vec_per_row = p.N / 8;
-      const long long total = static_cast<long long>(p.out_rows) * vec_per_row;
-      const long long stride = static_cast<long long>(gridDim.x) * 64;
-      const __nv_bfloat16* rb = p.recv[p.rank];
-      const long long slot = static_cast<long long>(p.seg_cap) * p.ldd;
-      for (long long v = static_cast<long long>(blockIdx.x) * 64 + (warp - 6) * 32 + lane;
-           v < total; v += stride) {
-        const int r = static_cast<int>(v / vec_per_row);
-        const int c = static_cast<int>(v % vec_per_row) * 8;
-        uint4* dst = reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c);
-        if (r >= rows) {
-          *dst = make_uint4(0u, 0u, 0u, 0u);
-          continue;
+    for (int blk = lo / S::BM; lo < hi && blk <= (hi - 1) / S::BM && ok; ++blk) {
+      if (lane == 0)
+        ok = tpc::wait_epoch(p.peer_flags[p.rank] + p.flag_blk + blk * p.P, p.P, p.epoch,
+                             abort_flag, p.err);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      const int r_a = max(lo, blk * S::BM), r_b = min(hi, blk * S::BM + S::BM);
+      const long long total = static_cast<long long>(r_b - r_a) * vec_per_row;
+      constexpr int U = 8;  // independent 16-byte reductions in flight per thread
+      for (long long v0 = t0; v0 < total; v0 += U * stride) {
+        uint4 red[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const long long v = v0 + u * stride;
+          if (v >= total) continue;
+          const long long off = static_cast<long long>(r_a + v / vec_per_row) * p.ldd +
+                                (v % vec_per_row) * 8;
+          if (p.mc_part) {
+            red[u] = tpc::ld_reduce_bf16x8(p.mc_part + off);
+          } else {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int q2 = 0; q2 < p.P; ++q2) {
+              const uint4 w4 = *reinterpret_cast<const uint4*>(p.peer_part[q2] + off);
+              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w4);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(h[e]);
+                acc[2 * e] += f.x;
+                acc[2 * e + 1] += f.y;
+              }
+            }
+            red[u] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+          }
         }
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const long long off = static_cast<long long>(r) * p.ldd + c;
-        for (int q2 = 0; q2 < p.P; ++q2) {
-          const uint4 w4 = *reinterpret_cast<const uint4*>(rb + q2 * slot + off);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w4);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const long long v = v0 + u * stride;
+          if (v >= total) continue;
+          const int r = r_a - lo + static_cast<int>(v / vec_per_row);  // row of out
+          const int c = static_cast<int>(v % vec_per_row) * 8;
+          float acc[8];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&red[u]);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = __bfloat1622float2(h[e]);
-            acc[2 * e] += f.x;
-            acc[2 * e + 1] += f.y;
+            acc[2 * e] = f.x;
+            acc[2 * e + 1] = f.y;
           }
-        }
-        if (p.rs_resid) {
-          const uint4 u4 =
-              *reinterpret_cast<const uint4*>(p.rs_resid + static_cast<long long>(r) * p.ld_resid + c);
-          const __nv_bfloat162* hr = reinterpret_cast<const __nv_bfloat162*>(&u4);
+          if (p.rs_resid) {
+            const uint4 u4 = *reinterpret_cast<const uint4*>(
+                p.rs_resid + static_cast<long long>(r) * p.ld_resid + c);
+            const __nv_bfloat162* hr = reinterpret_cast<const __nv_bfloat162*>(&u4);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(hr[e]);
-            acc[2 * e] += f.x;
-            acc[2 * e + 1] += f.y;
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __bfloat1622float2(hr[e]);
+              acc[2 * e] += f.x;
+              acc[2 * e + 1] += f.y;
+            }
           }
+          *reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c) =
+              make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                         pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
         }
-        *dst = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
       }
-      // this rank has read its receive slots: the last sum warp of the grid tells all ranks
-      // (their stores of epoch + 2 may reuse the slots)
+    }
+    if (ok) {
+      // padding rows of out
+      const long long zt = static_cast<long long>(max(0, p.out_rows - (hi - lo))) * vec_per_row;
+      for (long long v = t0; v < zt; v += stride) {
+        const int r = (hi - lo) + static_cast<int>(v / vec_per_row);
+        const int c = static_cast<int>(v % vec_per_row) * 8;
+        *reinterpret_cast<uint4*>(p.rs_out + static_cast<long long>(r) * p.ld_out + c) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+      // this rank has read its rows of every partial buffer: the last pull warp of the grid
+      // tells all ranks (their buffer of this epoch's parity may be rewritten at epoch + 2)
       __syncwarp();
       if (lane == 0) {
         __threadfence_system();
-        if (atomicAdd(p.tile_cnt + p.P, 1u) == 2u * gridDim.x - 1u) {
+        if (atomicAdd(p.tile_cnt + num_m, 1u) == 2u * gridDim.x - 1u) {
           for (int q2 = 0; q2 < p.P; ++q2)
             tpc::st_release_sys(p.peer_flags[q2] + p.flag_done + p.rank, p.epoch);
         }
@@ -562,9 +589,10 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
   if (warp == 1) tmem_dealloc(tmem_base, S::TMEM_COLS);
   if (TPM != 0 && threadIdx.x == 0) {
     // the last CTA to finish clears the local counters for the next launch
+    const int ncnt = TPM == 2 ? num_m + 2 : p.P + 2;
     __threadfence();
-    if (atomicAdd(p.tile_cnt + p.P + 1, 1u) == gridDim.x - 1u) {
-      for (int i = 0; i <= p.P + 1; ++i) atomicExch(p.tile_cnt + i, 0u);
+    if (atomicAdd(p.tile_cnt + ncnt - 1, 1u) == gridDim.x - 1u) {
+      for (int i = 0; i < ncnt; ++i) atomicExch(p.tile_cnt + i, 0u);
     }
   }
 }
@@ -720,8 +748,10 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.lda = lda;
   a.ag_mc = nullptr;
   a.ag_peers = nullptr;
-  a.recv = nullptr;
-  a.seg_cap = 0;
+  a.mc_part = nullptr;
+  a.peer_part = nullptr;
+  a.flag_blk = 0;
+  a.interleave_spb = 0;
   a.rs_resid = nullptr;
   a.rs_out = nullptr;
   a.ld_resid = a.ld_out = 0;
@@ -753,11 +783,14 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
 #undef CFB_TP1
       return -4;
     }
-    if (epi != kEpiBF16 || !tp->recv || !tp->out || (N % 8) || tp->out_rows < 0 ||
-        tp->seg_cap <= 0)
+    if (epi != kEpiBF16 || !tp->out || (N % 8) || tp->out_rows < 0 ||
+        (!tp->mc_part && !tp->peer_part))
       return -13;
-    a.recv = reinterpret_cast<__nv_bfloat16* const*>(tp->recv);
-    a.seg_cap = tp->seg_cap;
+    a.mc_part = static_cast<const __nv_bfloat16*>(tp->mc_part);
+    a.peer_part = reinterpret_cast<const __nv_bfloat16* const*>(tp->peer_part);
+    a.flag_blk = tp->flag_blk;
+    a.interleave_spb = tp->interleave_spb;
+    if (a.interleave_spb > 0 && (M != tp->P * a.interleave_spb * 128)) return -13;
     a.rs_resid = static_cast<const __nv_bfloat16*>(tp->resid);
     a.rs_out = static_cast<__nv_bfloat16*>(tp->out);
     a.ld_resid = tp->ld_resid;

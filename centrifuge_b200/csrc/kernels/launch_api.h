@@ -21,10 +21,12 @@ int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long lo
 //     per CTA copy it to every other rank's A (multicast store through the NVSwitch, or peer
 //     stores) and raise ready[rank] there, while the TMA producer reads other segments only
 //     after their ready flag (own segment first).
-//   mode 2 (reduce-scatter of D): the epilogue stores each row's partial sum into slot [rank]
-//     of the row owner's receive buffer (recv[o], rows of seg_cap); two extra warps per CTA
-//     add this rank's P slots once all ranks have signalled, plus `resid`, into `out` rows
-//     [0, count) and zero rows up to out_rows.  D itself is not written.
+//   mode 2 (reduce-scatter of D): D is this rank's partial buffer in symmetric memory; when an
+//     m-block is stored, its owners get blk_ready[m][rank] = epoch (at flag_blk); two extra
+//     warps per CTA of an owner reduce its segment block by block as soon as all ranks stored
+//     the block (multimem.ld_reduce on mc_part, or loads from peer_part), add `resid` and write
+//     `out` rows [0, count), zeros up to out_rows.  With interleave_spb > 0 (uniform segments of
+//     that many 128-row blocks) the m-blocks run interleaved across owners.
 struct CfbTpGemm {
   int mode;
   int rank, P;
@@ -32,12 +34,14 @@ struct CfbTpGemm {
   uint32_t epoch;
   uint32_t* const* peer_flags;    // device array [P] of flag buffers (symmetric memory)
   int flag_ready, flag_done;
-  uint32_t* tile_cnt;             // local scratch [P + 2], zero at rest
+  uint32_t* tile_cnt;             // local scratch [max(P, m-blocks) + 2], zero at rest
   int rot_rows;                   // mode 1: first row computed (multiple of 128)
   void* ag_mc;                    // mode 1: multicast address of A (or nullptr)
   void* const* ag_peers;          // mode 1: device array [P] of A on every rank
-  void* const* recv;              // mode 2: device array [P] of receive buffers
-  int seg_cap;                    // mode 2: rows per receive slot
+  const void* mc_part;            // mode 2: multicast address of D (or nullptr)
+  const void* const* peer_part;   // mode 2: device array [P] of D on every rank
+  int flag_blk;                   // mode 2: offset of blk_ready[num m-blocks][P]
+  int interleave_spb;             // mode 2: > 0 for uniform segments (m-blocks per segment)
   const void* resid;              // mode 2: [count, N] bf16 (optional)
   long long ld_resid;
   void* out;                      // mode 2: [out_rows, N] bf16

@@ -11,18 +11,20 @@ inside the GEMM kernel (``gemm_tp``, csrc/kernels/gemm_sm100.cu), in one coopera
   stores) and raise a ready flag there, while the tensor cores start on the local rows (the m
   blocks are rotated so the own segment comes first); the TMA producer reads another rank's
   rows only after its flag;
-* reduce-scatter (mode 2): the epilogue stores each partial row straight into slot [rank] of
-  the row owner's receive buffer over NVLink (overlapping the next tile's MMAs) and counts rows
-  per owner; when an owner's segment is complete everywhere, two extra warps per CTA of the
-  owner add its P slots (local reads) and the residual into the layer output.
+* reduce-scatter (mode 2): the epilogue writes partial tiles into this rank's symmetric partial
+  buffer and, when a 128-row block is complete, raises a per-block flag at the block's owners;
+  two extra warps per CTA of every owner reduce its rows block by block as soon as all ranks
+  have stored the block (``multimem.ld_reduce`` through the NVSwitch with fp32 accumulation, or
+  peer loads), add the residual and write the layer output.  In the forward (uniform shards)
+  the m-blocks are interleaved across owners so every owner pulls while the GEMM runs.
 
 Rows are split into per-rank segments (:class:`Segments`): uniform sequence-parallel shards in
 the forward, each rank's kept rows (compact global order) in the filtered backward, so the
 GEMMs see exactly the kept rows.  Buffers live in ``torch.distributed._symmetric_memory``.  The
 gather buffers are per call site ("slots", two per layer) and double as the saved activations
 of the backward, so a slot is rewritten only by the next micro-batch's forward; the receive
-buffers alternate by epoch and a GEMM of epoch e waits until every rank finished reading epoch
-e - 2.  Flags carry monotonically increasing epochs (never reset); every rank issues the same
+partial buffers alternate by epoch and a GEMM of epoch e waits until every rank finished
+reading epoch e - 2.  Flags carry monotonically increasing epochs (never reset); every rank issues the same
 sequence of fused calls, so epochs agree across the group.  All waits are bounded (20 s) and
 report through the kernels' error word.
 """
@@ -52,12 +54,14 @@ class TPFusedComm:
         self.pbuf = symm_mem.empty(2 * T * H, dtype=bf16, device=self.device)
         self.phdl = symm_mem.rendezvous(self.pbuf, tp.group)
         P = self.P
-        self.flags = symm_mem.empty(3 * P, dtype=torch.int32, device=self.device)
+        self.nblk = (T + 127) // 128
+        self.flags = symm_mem.empty(3 * P + self.nblk * P, dtype=torch.int32, device=self.device)
         self.flags.zero_()
         self.fhdl = symm_mem.rendezvous(self.flags, tp.group)
         self.peer_flags_dev = int(self.fhdl.buffer_ptrs_dev)
-        # flag layout: gather ready[P] at 0, reduce-scatter ready[P] at P, done[P] at 2P
-        self.off_rs_ready, self.off_rs_done = P, 2 * P
+        # flag layout: gather ready[P] at 0, (unused) [P] at P, reduce-scatter done[P] at 2P,
+        # reduce-scatter block ready[nblk][P] at 3P
+        self.off_rs_done, self.off_blk = 2 * P, 3 * P
         mc_ok = use_multicast and self.ghdl.has_multicast_support and self.phdl.has_multicast_support
         self.g_mc = int(self.ghdl.multicast_ptr) if mc_ok else 0
         self.p_mc = int(self.phdl.multicast_ptr) if mc_ok else 0
@@ -69,7 +73,7 @@ class TPFusedComm:
                                      device=self.device) for s in range(n_gather)]
         self.p_peers = [torch.tensor([b + i * T * H * esz for b in pb], dtype=torch.int64,
                                      device=self.device) for i in range(2)]
-        self.cnt = torch.zeros(P + 2, dtype=torch.int32, device=self.device)
+        self.cnt = torch.zeros(max(P, self.nblk) + 2, dtype=torch.int32, device=self.device)
         self.ag_epoch = 0
         self.rs_epoch = 0
         self._uniform = None
@@ -135,7 +139,7 @@ class TPFusedComm:
         kernels().gemm_tp(xg, w, out, b_mn, pos, table, rc, hd, 1, self.rank, self.P, seg.dev,
                           self.ag_epoch, self.peer_flags_dev, 0, 0, self.cnt, rot,
                           self._mc(self.g_mc, slot * T * H), self.g_peers[slot].data_ptr(), 0, 0,
-                          None, None)
+                          0, 0, None, None)
         return out
 
     # ---------------------------------------------------------------- reduce-scatter
@@ -149,20 +153,21 @@ class TPFusedComm:
         T = a.shape[0]
         N = w.shape[1] if b_mn else w.shape[0]
         assert T == seg.total and T <= self.T and N <= self.H
-        assert max(seg.counts) <= self.shard
         self.rs_epoch += 1
         e = self.rs_epoch
         i = e & 1
-        carrier = self.pbuf[i * self.T * self.H:i * self.T * self.H + max(T, 1) * N].view(-1, N)[:T]
+        part = self.pbuf[i * self.T * self.H:i * self.T * self.H + max(T, 1) * N].view(-1, N)[:T]
         rows = seg.counts[self.rank] if out_rows is None else out_rows
         if out is None:
             out = torch.empty(rows, N, dtype=a.dtype, device=self.device)
         if T == 0:
             out.zero_()
             return out
-        kernels().gemm_tp(a, w, carrier, b_mn, None, None, 0, 0, 2, self.rank, self.P, seg.dev,
-                          e, self.peer_flags_dev, self.off_rs_ready, self.off_rs_done, self.cnt,
-                          0, 0, 0, self.p_peers[i].data_ptr(), self.shard, resid, out)
+        spb = (self.shard // 128) if seg is self._uniform and T == self.T else 0
+        mc = self._mc(self.p_mc, i * self.T * self.H)
+        kernels().gemm_tp(a, w, part, b_mn, None, None, 0, 0, 2, self.rank, self.P, seg.dev, e,
+                          self.peer_flags_dev, 0, self.off_rs_done, self.cnt, 0, 0, 0, mc,
+                          self.p_peers[i].data_ptr(), self.off_blk, spb, resid, out)
         return out
 
 
