@@ -369,6 +369,22 @@ void adamw(Tensor& master, const Tensor& grad, Tensor& m, Tensor& v, Tensor& par
                "adamw");
 }
 
+// AdamW on a shard with the bf16 result written through the multicast address `param_mc` (raw
+// device address into symmetric memory): the ZeRO parameter all-gather fused into the step.
+void adamw_multicast(Tensor& master, const Tensor& grad, Tensor& m, Tensor& v, int64_t param_mc,
+                     double lr, double b1, double b2, double eps, double wd, double bc1,
+                     double bc2, const c10::optional<Tensor>& grad_scale) {
+  TORCH_CHECK(master.scalar_type() == at::kFloat && grad.scalar_type() == at::kFloat, "fp32");
+  const int64_t n = master.numel();
+  TORCH_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n, "n");
+  const c10::cuda::CUDAGuard guard(master.device());
+  CFB_CHECK_RC(cfb_adamw_multicast(master.data_ptr<float>(), grad.data_ptr<float>(),
+                                   m.data_ptr<float>(), v.data_ptr<float>(),
+                                   reinterpret_cast<void*>(param_mc), n, lr, b1, b2, eps, wd,
+                                   bc1, bc2, opt_ptr<float>(grad_scale), cur_stream()),
+               "adamw_multicast");
+}
+
 void sumsq(const Tensor& x, Tensor& partial) {
   TORCH_CHECK(x.scalar_type() == at::kFloat && partial.scalar_type() == at::kFloat, "fp32");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -607,6 +623,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse"), py::arg("dloss"), py::arg("dlogits"), py::arg("vocab_start") = 0);
   m.def("ce_partial", &ce_partial);
   m.def("adamw", &adamw);
+  m.def("adamw_multicast", &adamw_multicast);
   m.def("sumsq", &sumsq);
   m.def("clip_coef", &clip_coef);
   m.def("drop_smallest", &drop_smallest);

@@ -499,6 +499,10 @@ __global__ void __launch_bounds__(256) ce_bwd_kernel(
 }
 
 // ---------------------------------------------------------------- optimizer
+// MC: `param` is the NVSwitch multicast address of the data-parallel group's bf16 parameters,
+// so each updated value is written once and lands on every rank (the ZeRO parameter
+// all-gather fused into the optimizer step); n must then be a multiple of 4.
+template <bool MC = false>
 __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict__ grad,
                              float* __restrict__ m, float* __restrict__ v,
                              __nv_bfloat16* __restrict__ param, long long n, float lr,
@@ -533,10 +537,17 @@ __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict
     uint2 o;
     o.x = pack_bf16x2(p.x, p.y);
     o.y = pack_bf16x2(p.z, p.w);
-    reinterpret_cast<uint2*>(param)[i] = o;
+    if (MC) {
+      asm volatile("multimem.st.relaxed.sys.global.v2.f32 [%0], {%1, %2};" ::"l"(
+                       reinterpret_cast<uint2*>(param) + i),
+                   "f"(__uint_as_float(o.x)), "f"(__uint_as_float(o.y))
+                   : "memory");
+    } else {
+      reinterpret_cast<uint2*>(param)[i] = o;
+    }
   }
   // tail
-  if (blockIdx.x == 0 && threadIdx.x < (n & 3)) {
+  if (!MC && blockIdx.x == 0 && threadIdx.x < (n & 3)) {
     const long long j = n4 * 4 + threadIdx.x;
     const float gj = grad[j] * gs;
     float pj = master[j];
@@ -834,6 +845,17 @@ int cfb_adamw(float* master, const float* grad, float* m, float* v, void* param_
   if (n == 0) return 0;
   adamw_kernel<<<grid_for(n / 4 + 1, 256, 148 * 8), 256, 0, st>>>(
       master, grad, m, v, static_cast<bf16*>(param_bf16), n, lr, beta1, beta2, eps, wd, bc1, bc2,
+      grad_scale);
+  return last_err();
+}
+
+int cfb_adamw_multicast(float* master, const float* grad, float* m, float* v, void* param_mc,
+                        long long n, float lr, float beta1, float beta2, float eps, float wd,
+                        float bc1, float bc2, const float* grad_scale, cudaStream_t st) {
+  if (n == 0) return 0;
+  if (n % 4 || (reinterpret_cast<uintptr_t>(param_mc) & 7)) return -11;
+  adamw_kernel<true><<<grid_for(n / 4, 256, 148 * 8), 256, 0, st>>>(
+      master, grad, m, v, static_cast<bf16*>(param_mc), n, lr, beta1, beta2, eps, wd, bc1, bc2,
       grad_scale);
   return last_err();
 }

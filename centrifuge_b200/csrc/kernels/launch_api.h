@@ -89,6 +89,11 @@ int cfb_ce_partial(const void* logits, long long ld, const long long* labels, fl
 int cfb_adamw(float* master, const float* grad, float* m, float* v, void* param_bf16, long long n,
               float lr, float beta1, float beta2, float eps, float wd, float bc1, float bc2,
               const float* grad_scale, cudaStream_t st);
+// AdamW whose bf16 output goes to the NVSwitch multicast address `param_mc` of the parameter
+// buffer shared by the data-parallel group (every rank receives the updated shard).
+int cfb_adamw_multicast(float* master, const float* grad, float* m, float* v, void* param_mc,
+                        long long n, float lr, float beta1, float beta2, float eps, float wd,
+                        float bc1, float bc2, const float* grad_scale, cudaStream_t st);
 int cfb_sumsq(const float* x, long long n, float* out_partial, int nblocks, cudaStream_t st);
 int cfb_clip_coef(const float* partials, int n, float max_norm, float extra_scale, float* coef,
                   float* norm_out, cudaStream_t st);

@@ -62,6 +62,19 @@ class FlatParams:
                 n *= d
             self.grads[name] = self.grad[o:o + n].view(shape)
 
+    def rebind_data(self, buf: torch.Tensor) -> None:
+        """Move the parameter storage to ``buf`` (e.g. symmetric memory, so that the optimizer
+        can write every rank's copy); parameter views are re-created."""
+        assert buf.numel() == self.numel and buf.dtype == self.data.dtype
+        buf.copy_(self.data)
+        self.data = buf
+        for name, shape in self.specs.items():
+            o = self.offsets[name]
+            n = 1
+            for d in shape:
+                n *= d
+            self.params[name] = self.data[o:o + n].view(shape)
+
     def names(self) -> List[str]:
         return list(self.specs)
 

@@ -37,7 +37,18 @@ class SymmReducer:
         self.mc = int(self.hdl.multicast_ptr) if (use_multicast and
                                                   self.hdl.has_multicast_support) else 0
         self.peer_ptrs_dev = int(self.hdl.buffer_ptrs_dev)
-        nflags = MAX_BUCKETS * self.W + self.W
+        # parameters in symmetric memory with an NVSwitch multicast mapping: the optimizer's
+        # AdamW writes each updated bf16 value once for the whole group (the ZeRO parameter
+        # all-gather fused into the step, ``adamw_all_gather``)
+        self.pmc = 0
+        if self.mc:
+            pbuf = symm_mem.empty(flat.numel, dtype=flat.data.dtype, device=dev)
+            flat.rebind_data(pbuf)
+            self.phdl = symm_mem.rendezvous(pbuf, group)
+            if self.phdl.has_multicast_support:
+                self.pmc = int(self.phdl.multicast_ptr)
+        self.p_epoch = 0
+        nflags = MAX_BUCKETS * self.W + 2 * self.W
         self.flags = symm_mem.empty(nflags, dtype=torch.int32, device=dev)
         self.flags.zero_()
         self.fhdl = symm_mem.rendezvous(self.flags, group)
@@ -71,6 +82,24 @@ class SymmReducer:
         k.symm_wait(self.flags.data_ptr(), base, 1, self.W, self.epoch, self.err)
         flat.grad.zero_()
         self.epoch += 1
+
+    def adamw_all_gather(self, opt, coef: torch.Tensor) -> None:
+        """AdamW on this rank's shard, bucket by bucket, with every updated bf16 parameter
+        stored through the multicast address (all ranks receive it); then a bounded flag
+        exchange orders the new parameters before anybody's next forward."""
+        k = kernels()
+        b1, b2 = opt.betas
+        bc1 = 1.0 - b1 ** opt.step_count
+        bc2 = 1.0 - b2 ** opt.step_count
+        for b in opt.buckets:
+            lo, hi = b.shard_off, b.shard_off + b.chunk
+            k.adamw_multicast(opt.master[lo:hi], opt.grad_shard[lo:hi], opt.m[lo:hi],
+                              opt.v[lo:hi], self.pmc + b.own_lo * 2, opt.lr, b1, b2, opt.eps,
+                              opt.wd, bc1, bc2, coef)
+        self.p_epoch += 1
+        base = MAX_BUCKETS * self.W + self.W
+        k.symm_signal(self.peer_flags_dev, self.W, base + self.rank, self.p_epoch)
+        k.symm_wait(self.flags.data_ptr(), base, 1, self.W, self.p_epoch, self.err)
 
     def all_gather(self, dst: torch.Tensor, src_chunk: torch.Tensor) -> None:
         dist.all_gather_into_tensor(dst, src_chunk, group=self.group)

@@ -251,6 +251,10 @@ class ZeroAdamW:
                                       partial=self._sumsq)
         coef = self._coef if g.is_cuda else float(self._coef.item())
         b1, b2 = self.betas
+        if self.W > 1 and getattr(self.reducer, "pmc", 0):
+            # parameter all-gather fused into AdamW (NVSwitch multicast stores)
+            self.reducer.adamw_all_gather(self, coef)
+            return self._norm
         fused.adamw_(self.master, g, self.m, self.v, self.param_out, self.lr, b1, b2, self.eps,
                      self.wd, self.step_count, coef)
         if self.W > 1:
