@@ -120,6 +120,26 @@ void gemm_rope(const Tensor& a, const Tensor& b, Tensor& out, const Tensor& pos,
                "gemm_rope");
 }
 
+// gu [M, 2F] = x @ w^T (w = [gate; up] [2F, K]) and h [M, F] = silu(gate) * up in the epilogue
+void gemm_swiglu(const Tensor& x, const Tensor& w, Tensor& gu, Tensor& h) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(gu, "gu");
+  check_bf16_2d(h, "h");
+  const int64_t M = x.size(0), K = x.size(1), F2 = w.size(0);
+  TORCH_CHECK(w.size(1) == K && F2 % 2 == 0, "gemm_swiglu: w must be [2F, K]");
+  TORCH_CHECK(gu.size(0) == M && gu.size(1) == F2 && h.size(0) == M && h.size(1) == F2 / 2,
+              "gemm_swiglu: outputs");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_gemm_swiglu(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                               gu.data_ptr(), gu.stride(0), h.data_ptr(), h.stride(0),
+                               static_cast<int>(M), static_cast<int>(F2 / 2),
+                               static_cast<int>(K), err_word(x.get_device()).data_ptr<int>(),
+                               cur_stream()),
+               "gemm_swiglu");
+}
+
 // ---- tensor-parallel fusion (pointers into symmetric memory are raw device addresses)
 // out = a @ b^T (a @ b with b_mn) fused with a sequence-parallel collective over NVLink:
 // mode 1 all-gathers this rank's rows of `a` to every rank while computing, mode 2 writes the
@@ -599,6 +619,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("resid") = py::none(),
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
+  m.def("gemm_swiglu", &gemm_swiglu, "gate/up projection with the SwiGLU epilogue");
   m.def("gemm_tp", &gemm_tp, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("b_mn"),
         py::arg("pos"), py::arg("table"), py::arg("rope_cols"), py::arg("hd"), py::arg("mode"),
         py::arg("rank"), py::arg("P"), py::arg("seg"), py::arg("epoch"),

@@ -37,6 +37,11 @@ struct GemmArgs {
   const int* pos;
   const float* cs;
   int rope_cols, hd;
+  // kEpiSwiGLU: B rows [n, n + N) are the gate, rows dual_off + n the up projection; D [M, 2F]
+  // receives gate at column n and up at column dual_off + n, aux [M, F] (ld_aux) silu(g) * u
+  int dual_off;
+  __nv_bfloat16* aux;
+  long long ld_aux;
   // ---- tensor-parallel fusion.  Row segments: rank q owns rows [seg[q], seg[q+1]) of A / D
   // (device array [P + 1]; uniform shards in the forward, kept rows in the backward).  Flags
   // live in symmetric buffers peer_flags[q]: ready[P] at flag_ready, done[P] at flag_done.
@@ -117,16 +122,21 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v
 }
 }  // namespace tpc
 
-template <int BN>
+// DUAL (the SwiGLU epilogue): every stage also holds the B tile dual_off rows further down
+// (the up projection next to the gate), and each accumulator buffer has two BN-column halves.
+template <int BN, bool DUAL = false>
 struct GemmShape {
   static constexpr int BM = 128;
   static constexpr int BK = 64;
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int B1_BYTES = BN * BK * 2;
+  static constexpr int B_BYTES = (DUAL ? 2 : 1) * B1_BYTES;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int STAGES = (STAGE_BYTES >= 48 * 1024) ? 4 : 6;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-  static constexpr int TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  static constexpr int ACC_COLS = (DUAL ? 2 : 1) * BN;  // one accumulator buffer
+  static constexpr int TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64 ? 64 : (2 * ACC_COLS <= 128 ? 128 : (2 * ACC_COLS <= 256 ? 256 : 512)));
+  static_assert(2 * ACC_COLS <= 512, "TMEM");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& tm, int& tn) {
@@ -146,7 +156,8 @@ template <int BN, bool A_MN, bool B_MN, int EPI, int TPM = 0>
 __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
     gemm_bf16_sm100(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
-  using S = GemmShape<BN>;
+  constexpr bool DUAL = EPI == kEpiSwiGLU;
+  using S = GemmShape<BN, DUAL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -245,6 +256,7 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
           }
           if (!B_MN) {
             tma_load_2d(sb, &tmB, fb, k0, n0);
+            if (DUAL) tma_load_2d(sb + S::B1_BYTES, &tmB, fb, k0, n0 + p.dual_off);
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &tmB, fb, n0 + c * 64, k0);
@@ -279,7 +291,7 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, kErrWaitMma)) {
             ok = false;
@@ -295,6 +307,9 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
             const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024)
                                      : sdesc_sw128(sb + k * 32, 16, 1024);
             umma_bf16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            if (DUAL)
+              umma_bf16_ss(d_tmem + BN, ad, sdesc_sw128(sb + S::B1_BYTES + k * 32, 16, 1024), IDESC,
+                           (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(smem_u32(&empty[stage]));
           if (++stage == S::STAGES) {
@@ -336,12 +351,45 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
         break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * S::ACC_COLS;
       __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int col = n0 + c * 32;
         if (col >= p.N) break;  // warp-uniform
+        if (DUAL) {
+          uint32_t rg[32], ru[32];
+          CFB_TMEM_LD32(taddr + c * 32, rg);
+          CFB_TMEM_LD32(taddr + BN + c * 32, ru);
+          tmem_ld_wait();
+          if (row < p.M) {
+            uint32_t og[16], ou[16], oh[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              const float g0 = __uint_as_float(rg[2 * t]) * p.alpha;
+              const float g1 = __uint_as_float(rg[2 * t + 1]) * p.alpha;
+              const float u0 = __uint_as_float(ru[2 * t]) * p.alpha;
+              const float u1 = __uint_as_float(ru[2 * t + 1]) * p.alpha;
+              og[t] = pack_bf16x2(g0, g1);
+              ou[t] = pack_bf16x2(u0, u1);
+              // silu of the bf16-rounded gate, as a separate SwiGLU pass over gu would see it
+              const float2 gr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&og[t]));
+              const float2 ur = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ou[t]));
+              oh[t] = pack_bf16x2(gr.x / (1.f + __expf(-gr.x)) * ur.x,
+                                  gr.y / (1.f + __expf(-gr.y)) * ur.y);
+            }
+            __nv_bfloat16* gd = drow + col;
+            __nv_bfloat16* ud = drow + p.dual_off + col;
+            __nv_bfloat16* hd = p.aux + row * p.ld_aux + col;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              reinterpret_cast<uint4*>(gd)[j] = make_uint4(og[4 * j], og[4 * j + 1], og[4 * j + 2], og[4 * j + 3]);
+              reinterpret_cast<uint4*>(ud)[j] = make_uint4(ou[4 * j], ou[4 * j + 1], ou[4 * j + 2], ou[4 * j + 3]);
+              reinterpret_cast<uint4*>(hd)[j] = make_uint4(oh[4 * j], oh[4 * j + 1], oh[4 * j + 2], oh[4 * j + 3]);
+            }
+          }
+          continue;
+        }
         if (EPI == kEpiBF16Rope && col < p.rope_cols) {
           // the first-half chunk of a head rotates together with its partner hd/2 columns on
           const int half = p.hd >> 1;
@@ -641,7 +689,7 @@ static int num_sms() {
 template <int BN, bool A_MN, bool B_MN, int EPI, int TPM = 0>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                        cudaStream_t st, int max_ctas) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, EPI == kEpiSwiGLU>;
   auto kern = gemm_bf16_sm100<BN, A_MN, B_MN, EPI, TPM>;
   static bool configured = false;
   if (!configured) {
@@ -737,6 +785,9 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.cs = cs;
   a.rope_cols = rope_cols;
   a.hd = hd;
+  a.dual_off = 0;
+  a.aux = nullptr;
+  a.ld_aux = 0;
   a.rank = 0;
   a.P = 1;
   a.seg = nullptr;
@@ -822,6 +873,34 @@ int cfb_gemm_bf16_rope(const void* A, long long lda, const void* B, long long ld
   if (reinterpret_cast<uintptr_t>(cos_sin) & 15) return -12;
   return gemm_entry(A, lda, 0, B, ldb, 0, D, ldd, kEpiBF16Rope, nullptr, 0, M, N, K, 1.0f, err,
                     bn, max_ctas, pos, cos_sin, rope_cols, head_dim, nullptr, st);
+}
+
+int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, void* GU,
+                    long long ld_gu, void* Hout, long long ld_h, int M, int F, int K, int* err,
+                    cudaStream_t st) {
+  if (M <= 0 || F <= 0 || K <= 0) return -10;
+  if ((F % 128) || (lda % 8) || (ldb % 8) || (ld_gu % 8) || (ld_h % 8)) return -11;
+  if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (reinterpret_cast<uintptr_t>(GU) & 15) || (reinterpret_cast<uintptr_t>(Hout) & 15))
+    return -12;
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d_bf16(&ta, A, M, K, lda, 64, 128);
+  if (rc) return rc * 100 - 1;
+  rc = make_tmap_2d_bf16(&tb, B, 2LL * F, K, ldb, 64, 128);
+  if (rc) return rc * 100 - 2;
+  GemmArgs a = {};
+  a.M = M;
+  a.N = F;
+  a.K = K;
+  a.D = GU;
+  a.ldd = ld_gu;
+  a.alpha = 1.0f;
+  a.err = err;
+  a.dual_off = F;
+  a.aux = static_cast<__nv_bfloat16*>(Hout);
+  a.ld_aux = ld_h;
+  a.P = 1;
+  return launch_gemm<128, false, false, kEpiSwiGLU>(ta, tb, a, st, 0);
 }
 
 int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,

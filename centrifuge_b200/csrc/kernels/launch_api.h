@@ -6,12 +6,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3, kEpiBF16Rope = 4 };
+enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3, kEpiBF16Rope = 4, kEpiSwiGLU = 5 };
 
 // GEMM (gemm_sm100.cu): D = alpha * op(A) op(B) with the epilogue `epi`.
 int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
                   int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st);
+// Gate/up projection with SwiGLU in the epilogue: B = [gate; up] [2F, K] (K-major), both halves
+// computed per tile (two TMEM accumulators); GU [M, 2F] receives [g | u] (kept for the
+// backward), Hout [M, F] silu(g) * u.  F must be a multiple of 128.
+int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, void* GU,
+                    long long ld_gu, void* Hout, long long ld_h, int M, int F, int K, int* err,
+                    cudaStream_t st);
+
 // Tensor-parallel fusion of a GEMM (A [M, K] K-major; B [N, K] K-major or, with b_mn, [K, N])
 // with a collective over NVLink (gemm_sm100.cu), in one cooperative launch.  The M rows are
 // split into per-rank segments seg[q]..seg[q+1] (device array [P + 1]; uniform

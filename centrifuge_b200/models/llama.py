@@ -170,8 +170,7 @@ class LlamaCore(torch.nn.Module):
             o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd, scale=self.scale)
             x2 = G.linear_fwd(o, p[pre + "wo"], resid=x)
             xn2, rstd2 = fused.rmsnorm_fwd(x2, p[pre + "ln2"], cfg.rms_norm_eps)
-            gu = G.linear_fwd(xn2, p[pre + "wgu"])
-            h = fused.swiglu_fwd(gu)
+            gu, h = G.linear_fwd_swiglu(xn2, p[pre + "wgu"])  # SwiGLU in the epilogue
             x = G.linear_fwd(h, p[pre + "wd"], resid=x2)
             L.update(xn=xn, rstd1=rstd1, qkv=qkv, o=o, lse=lse, x2=x2, xn2=xn2, rstd2=rstd2,
                      gu=gu, h=h)

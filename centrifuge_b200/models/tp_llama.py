@@ -172,8 +172,7 @@ class TPLlamaCore(torch.nn.Module):
             x2 = tp.reduce_scatter_rows(part) + x if P > 1 else G.linear_fwd(o, p[pre + "wo"], resid=x)
             xn2_p, r2 = fused.rmsnorm_fwd(x2, p[pre + "ln2"], cfg.rms_norm_eps)
             xn2 = tp.all_gather_rows(xn2_p)
-            gu = G.linear_fwd(xn2, p[pre + "wgu"])
-            h = fused.swiglu_fwd(gu)
+            gu, h = G.linear_fwd_swiglu(xn2, p[pre + "wgu"])  # SwiGLU in the epilogue
             x = tp.reduce_scatter_rows(G.linear_fwd(h, p[pre + "wd"])) + x2 if P > 1 else \
                 G.linear_fwd(h, p[pre + "wd"], resid=x2)
             L.update(xn=xn, rstd1=r1, qkv=qkv, o=o, lse=lse, x2=x2, xn2=xn2, rstd2=r2, gu=gu, h=h)

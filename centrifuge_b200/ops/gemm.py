@@ -66,6 +66,21 @@ def linear_fwd_rope(x: torch.Tensor, w: torch.Tensor, pos: torch.Tensor, table: 
     return out
 
 
+def linear_fwd_swiglu(x: torch.Tensor, w: torch.Tensor):
+    """``gu = x w^T`` for ``w = [gate; up]`` and ``h = silu(gate) * up`` from the same kernel
+    (SwiGLU in the GEMM epilogue).  Returns ``(gu [T, 2F], h [T, F])``; ``gu`` is what the
+    backward needs."""
+    F = w.shape[0] // 2
+    gu = torch.empty(x.shape[0], 2 * F, dtype=x.dtype, device=x.device)
+    h = torch.empty(x.shape[0], F, dtype=x.dtype, device=x.device)
+    if not x.is_cuda or F % 128:
+        gu = gemm(x, w, gu, False, False)
+        from . import fused
+        return gu, fused.swiglu_fwd(gu, out=h)
+    kernels().gemm_swiglu(x, w, gu, h)
+    return gu, h
+
+
 def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
                  resid: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:

@@ -199,6 +199,20 @@ def test_attention_fwd(B, S, nh, nkv, hd):
     assert rel_err(o2, o) < 1e-2 and rel_err(l2, lse) < 1e-4
 
 
+@pytest.mark.parametrize("M,F,K", [(4096, 5632, 2048), (1000, 256, 512), (333, 1792, 4096)])
+def test_gemm_swiglu_epilogue(M, F, K):
+    """Gate/up projection with SwiGLU in the epilogue vs the projection + SwiGLU pass."""
+    torch.manual_seed(14)
+    x = torch.randn(M, K, device=dev).bfloat16()
+    w = (torch.randn(2 * F, K, device=dev) / K ** 0.5).bfloat16()
+    gu, h = gemm.linear_fwd_swiglu(x, w)
+    y = x.float() @ w.float().t()
+    assert rel_err(gu, y) < 1e-2
+    assert rel_err(h, ref.swiglu(y)) < 2e-2
+    h2 = fused.swiglu_fwd(gu)
+    assert (h.float() - h2.float()).abs().max().item() < 2e-2 * max(1.0, h2.float().abs().max().item())
+
+
 @pytest.mark.parametrize("M,nh,nkv,hd,bn", [(4096, 32, 4, 64, 0), (1000, 8, 2, 128, 128),
                                             (333, 4, 4, 64, 256), (2048, 16, 8, 128, 256)])
 def test_gemm_rope_epilogue(M, nh, nkv, hd, bn):
