@@ -15,7 +15,12 @@ import torch
 from centrifuge_b200.ops import fused, gemm
 
 
-def _time(fn, iters=20, warmup=5):
+ITERS, WARMUP = 20, 5
+
+
+def _time(fn, iters=None, warmup=None):
+    iters = ITERS if iters is None else iters
+    warmup = WARMUP if warmup is None else warmup
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -28,16 +33,23 @@ def _time(fn, iters=20, warmup=5):
     return s.elapsed_time(e) / iters
 
 
-def bench_gemm(shapes):
+def bench_gemm(shapes, bn=0, cublas=True):
     rows = []
     for (M, N, K, a_mn, b_mn, name) in shapes:
         A = torch.randn(K, M, device="cuda").bfloat16() if a_mn else torch.randn(M, K, device="cuda").bfloat16()
         B = torch.randn(K, N, device="cuda").bfloat16() if b_mn else torch.randn(N, K, device="cuda").bfloat16()
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        ms = _time(lambda: gemm.gemm(A, B, out, a_mn, b_mn, gemm.EPI_BF16))
+        if a_mn and b_mn:
+            # weight gradient: fp32 accumulation into the gradient buffer (split-K when the
+            # tile count leaves the last wave mostly empty)
+            out = torch.zeros(M, N, device="cuda", dtype=torch.float32)
+            epi = gemm.EPI_F32_ACC
+        else:
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            epi = gemm.EPI_BF16
+        ms = _time(lambda: gemm.gemm(A, B, out, a_mn, b_mn, epi, bn=bn))
         Am = A.t() if a_mn else A
         Bm = B if b_mn else B.t()
-        ms_ref = _time(lambda: torch.matmul(Am, Bm))
+        ms_ref = _time(lambda: torch.matmul(Am, Bm)) if cublas else float("nan")
         fl = 2.0 * M * N * K
         rows.append({"name": name, "M": M, "N": N, "K": K, "a_mn": a_mn, "b_mn": b_mn,
                      "ms": ms, "tflops": fl / ms / 1e9, "cublas_ms": ms_ref,
@@ -101,6 +113,11 @@ def main():
     ap.add_argument("--skip-gemm", action="store_true")
     ap.add_argument("--attn-shape", default="4,4096,32,8,128",
                     help="B,S,nh,nkv,hd of the attention benchmark")
+    ap.add_argument("--shapes", default=None, help="comma-separated GEMM shape names")
+    ap.add_argument("--bn", type=int, default=0, help="GEMM tile width (128, 256; 0 = auto)")
+    ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--keeps", default="1.0,0.7,0.5,0.3",
                     help="kept fractions of the filtered attention backward benchmark")
     args = ap.parse_args()
@@ -111,11 +128,19 @@ def main():
         (16384, 2048, 5632, False, False, "tinyllama_down_fwd"),
         (8192, 2048, 5632, False, True, "tinyllama_down_dgrad_kept"),
         (2048, 5632, 8192, True, True, "tinyllama_down_wgrad_kept"),
+        (2560, 2048, 8192, True, True, "tinyllama_qkv_wgrad_kept"),
+        (2048, 2048, 8192, True, True, "tinyllama_o_wgrad_kept"),
+        (11264, 2048, 8192, True, True, "tinyllama_gateup_wgrad_kept"),
         (16384, 32000, 2048, False, False, "tinyllama_lmhead_fwd"),
     ]
+    global ITERS, WARMUP
+    ITERS, WARMUP = args.iters, args.warmup
+    if args.shapes:
+        keep = set(args.shapes.split(","))
+        shapes = [sh for sh in shapes if sh[-1] in keep]
     out = {}
     if not args.skip_gemm:
-        out["gemm"] = bench_gemm(shapes)
+        out["gemm"] = bench_gemm(shapes, bn=args.bn, cublas=not args.no_cublas)
     if not args.skip_attn:
         B, S, nh, nkv, hd = (int(x) for x in args.attn_shape.split(","))
         keeps = tuple(float(x) for x in args.keeps.split(","))

@@ -14,18 +14,23 @@
 //   warp 1  MMA issuer:   tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators
 //   warps 2-5 epilogue:   tcgen05.ld of the accumulator, fused epilogue, global stores
 // The two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i overlap the
-// MMAs of tile i+1.  Every mbarrier wait is bounded (see sm100_common.cuh); on timeout the
+// MMAs of tile i+1.  Weight-gradient GEMMs (fp32 accumulate into the gradient) may split K so
+// that the number of work units fills whole waves of the 148 SMs.  Every mbarrier wait is bounded (see sm100_common.cuh); on timeout the
 // kernel records an error code, drains its own in-flight work and frees TMEM.
 #include "sm100_common.cuh"
 #include "launch_api.h"
 
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 
 namespace cfb {
 
 struct GemmArgs {
   int M, N, K;
+  // split-K (kEpiF32Acc only): every output tile is computed as ksplit work units over
+  // consecutive k-block ranges, each adding its partial sum into D with fp32 vector reductions
+  int ksplit;
   void* D;
   long long ldd;
   const __nv_bfloat16* R;
@@ -176,6 +181,8 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + S::BK - 1) / S::BK;
+  const int ksplit = p.ksplit;
+  const int num_units = num_tiles * ksplit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -213,7 +220,8 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       uint32_t last_phase = 0;
       bool ok = true;
       uint64_t ready_mask = 0;  // TPM 1: shards known to be gathered
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        const int tile = unit / ksplit, ks = unit - tile * ksplit;
         int tm, tn;
         tile_coords(tile, num_m, num_n, tm, tn);
         if (TPM == 2 && p.interleave_spb > 0) tm = (tm % p.P) * p.interleave_spb + tm / p.P;
@@ -237,7 +245,8 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
           if (waited) asm volatile("fence.proxy.async.global;" ::: "memory");
         }
         const int m0 = tm * S::BM, n0 = tn * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb_end = (ks + 1) * num_kb / ksplit;
+        for (int kb = ks * num_kb / ksplit; kb < kb_end; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err,
                          kErrWaitProducer)) {
             ok = false;
@@ -283,7 +292,9 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x, ++it) {
+        const int ks = unit % ksplit;
+        const int kb_beg = ks * num_kb / ksplit, kb_end = (ks + 1) * num_kb / ksplit;
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err, kErrWaitMma)) {
@@ -292,7 +303,7 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb_beg; kb < kb_end; ++kb) {
           if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, kErrWaitMma)) {
             ok = false;
             break;
@@ -306,10 +317,11 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
                                      : sdesc_sw128(sa + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024)
                                      : sdesc_sw128(sb + k * 32, 16, 1024);
-            umma_bf16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            const uint32_t accum = (kb != kb_beg || k != 0) ? 1u : 0u;
+            umma_bf16_ss(d_tmem, ad, bd, IDESC, accum);
             if (DUAL)
               umma_bf16_ss(d_tmem + BN, ad, sdesc_sw128(sb + S::B1_BYTES + k * 32, 16, 1024), IDESC,
-                           (kb | k) != 0 ? 1u : 0u);
+                           accum);
           }
           umma_commit(smem_u32(&empty[stage]));
           if (++stage == S::STAGES) {
@@ -338,8 +350,9 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
                               p.err);
       (void)__shfl_sync(0xffffffffu, okw ? 1 : 0, 0);  // on timeout abort_flag is raised
     }
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++it) {
       if (TPM == 2 && *abort_flag) break;
+      const int tile = unit / ksplit;
       int tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
       if (TPM == 2 && p.interleave_spb > 0) tm = (tm % p.P) * p.interleave_spb + tm / p.P;
@@ -463,6 +476,14 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              if (EPI == kEpiF32Acc && ksplit > 1) {
+                // the k-splits of this tile add into D concurrently (fp32, order not fixed)
+                asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                                 d4 + j),
+                             "f"(o.x), "f"(o.y), "f"(o.z), "f"(o.w)
+                             : "memory");
+                continue;
+              }
               if (EPI == kEpiF32Acc) {
                 const float4 old = d4[j];
                 o.x += old.x;
@@ -696,7 +717,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmA
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
     configured = true;
   }
-  const int tiles = ((a.M + 127) / 128) * ((a.N + BN - 1) / BN);
+  const int tiles = ((a.M + 127) / 128) * ((a.N + BN - 1) / BN) * a.ksplit;
   int grid = tiles < num_sms() ? tiles : num_sms();
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
   if (TPM != 0) {
@@ -748,6 +769,40 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
 
 using namespace cfb;
 
+// Tile width and split-K factor of a weight-gradient GEMM (fp32 accumulate into D).  The K
+// (token) dimension is long and M x N (the weight) often yields a tile count just above a
+// multiple of the SM count, leaving most SMs idle in the last wave; splitting K into s ranges
+// multiplies the work units by s.  Picks the (bn, s) with the best wave efficiency
+// units / (waves * SMs), s <= 4 and at least 16 k-blocks of 64 per unit, preferring bn = 256
+// (less L2 -> smem traffic per FLOP) and the smallest s within 0.03 of the best.
+static void choose_split_k(int M, int N, int K, int& bn, int& ksplit) {
+  const int sms = num_sms();
+  const int num_kb = (K + 63) / 64;
+  const int bns[2] = {256, 128};
+  double best = -1.0;
+  int best_bn = 256, best_s = 1;
+  for (int b : bns) {
+    if ((bn == 128 || bn == 256) && b != bn) continue;
+    if (b == 256 && N <= 128) continue;
+    const long long tiles = ((M + 127LL) / 128) * ((N + b - 1LL) / b);
+    for (int s = 1; s <= 4; ++s) {
+      if (s > 1 && num_kb / s < 16) break;
+      const long long units = tiles * s;
+      const long long waves = (units + sms - 1) / sms;
+      double eff = static_cast<double>(units) / static_cast<double>(waves * sms);
+      if (b == 128) eff -= 0.05;  // more operand traffic per FLOP than bn = 256
+      eff -= 0.01 * (s - 1);      // fp32 reduction traffic of the extra splits
+      if (eff > best + 0.03) {
+        best = eff;
+        best_bn = b;
+        best_s = s;
+      }
+    }
+  }
+  bn = best_bn;
+  ksplit = best_s;
+}
+
 static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, long long ldb,
                       int b_mn, void* D, long long ldd, int epi, const void* R, long long ldr,
                       int M, int N, int K, float alpha, int* err, int bn, int max_ctas,
@@ -758,7 +813,15 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (reinterpret_cast<uintptr_t>(D) & 15))
     return -12;
-  if (bn != 128 && bn != 256) {
+  int ksplit = 1;
+  // CFB_GEMM_SPLIT_K=0 keeps one unit per tile (fixed fp32 summation order)
+  static const bool split_k_on = [] {
+    const char* e = std::getenv("CFB_GEMM_SPLIT_K");
+    return !(e && e[0] == '0');
+  }();
+  if (epi == kEpiF32Acc && !tp && max_ctas <= 0 && (ldd % 4) == 0 && split_k_on) {
+    choose_split_k(M, N, K, bn, ksplit);
+  } else if (bn != 128 && bn != 256) {
     const long long tiles256 = ((M + 127LL) / 128) * ((N + 255LL) / 256);
     bn = (N <= 128 || tiles256 < num_sms()) ? 128 : 256;
   }
@@ -775,6 +838,7 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.M = M;
   a.N = N;
   a.K = K;
+  a.ksplit = ksplit;
   a.D = D;
   a.ldd = ldd;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
@@ -892,6 +956,7 @@ int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, 
   a.M = M;
   a.N = F;
   a.K = K;
+  a.ksplit = 1;
   a.D = GU;
   a.ldd = ld_gu;
   a.alpha = 1.0f;
