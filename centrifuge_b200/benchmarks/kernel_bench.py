@@ -16,6 +16,18 @@ from centrifuge_b200.ops import fused, gemm
 
 
 ITERS, WARMUP = 20, 5
+LAST_SM_MHZ = [None]
+
+
+def _sm_mhz():
+    """SM clock of device 0 now (NVML), or None."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        return pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+    except Exception:  # pragma: no cover - NVML missing
+        return None
 
 
 def _time(fn, iters=None, warmup=None):
@@ -29,11 +41,12 @@ def _time(fn, iters=None, warmup=None):
     for _ in range(iters):
         fn()
     e.record()
+    LAST_SM_MHZ[0] = _sm_mhz()  # read while the queued launches still run
     torch.cuda.synchronize()
     return s.elapsed_time(e) / iters
 
 
-def bench_gemm(shapes, bn=0, cublas=True):
+def bench_gemm(shapes, bn=0, cublas=True, compare=False):
     rows = []
     for (M, N, K, a_mn, b_mn, name) in shapes:
         A = torch.randn(K, M, device="cuda").bfloat16() if a_mn else torch.randn(M, K, device="cuda").bfloat16()
@@ -47,13 +60,20 @@ def bench_gemm(shapes, bn=0, cublas=True):
             out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
             epi = gemm.EPI_BF16
         ms = _time(lambda: gemm.gemm(A, B, out, a_mn, b_mn, epi, bn=bn))
+        mhz = LAST_SM_MHZ[0]
+        # the other tile shapes, timed back to back with the chosen one (same clock regime)
+        alt = {}
+        for bn_alt in (128, 256, 512):
+            if bn_alt != bn and compare:
+                t = _time(lambda: gemm.gemm(A, B, out, a_mn, b_mn, epi, bn=bn_alt))
+                alt[f"tflops_bn{bn_alt}"] = 2.0 * M * N * K / t / 1e9
         Am = A.t() if a_mn else A
         Bm = B if b_mn else B.t()
         ms_ref = _time(lambda: torch.matmul(Am, Bm)) if cublas else float("nan")
         fl = 2.0 * M * N * K
         rows.append({"name": name, "M": M, "N": N, "K": K, "a_mn": a_mn, "b_mn": b_mn,
-                     "ms": ms, "tflops": fl / ms / 1e9, "cublas_ms": ms_ref,
-                     "cublas_tflops": fl / ms_ref / 1e9})
+                     "ms": ms, "tflops": fl / ms / 1e9, "sm_mhz": mhz, "cublas_ms": ms_ref,
+                     "cublas_tflops": fl / ms_ref / 1e9, **alt})
         print(json.dumps(rows[-1]))
     return rows
 
@@ -116,6 +136,8 @@ def main():
     ap.add_argument("--shapes", default=None, help="comma-separated GEMM shape names")
     ap.add_argument("--bn", type=int, default=0, help="GEMM tile width (128, 256; 0 = auto)")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--compare-tiles", action="store_true",
+                    help="also time every fixed tile shape (bn 128, 256, 512 = CTA pair)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--keeps", default="1.0,0.7,0.5,0.3",
@@ -140,7 +162,8 @@ def main():
         shapes = [sh for sh in shapes if sh[-1] in keep]
     out = {}
     if not args.skip_gemm:
-        out["gemm"] = bench_gemm(shapes, bn=args.bn, cublas=not args.no_cublas)
+        out["gemm"] = bench_gemm(shapes, bn=args.bn, cublas=not args.no_cublas,
+                                 compare=args.compare_tiles)
     if not args.skip_attn:
         B, S, nh, nkv, hd = (int(x) for x in args.attn_shape.split(","))
         keeps = tuple(float(x) for x in args.keeps.split(","))

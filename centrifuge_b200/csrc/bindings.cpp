@@ -665,4 +665,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("EPI_BF16_RESID") = static_cast<int>(kEpiBF16Resid);
   m.attr("EPI_F32") = static_cast<int>(kEpiF32);
   m.attr("EPI_F32_ACC") = static_cast<int>(kEpiF32Acc);
+  m.attr("GEMM_TILE_PAIR") = static_cast<int>(kGemmTilePair);
 }

@@ -155,6 +155,147 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   tn = r / gsize;
 }
 
+// Epilogue of one accumulator row (TMEM lane) of a 128 x BN tile: tcgen05.ld of the fp32
+// accumulator at `taddr` (this warp's lane quadrant), then the EPI-specific conversion and
+// global stores of row `row`, columns [n0, n0 + BN) (clipped to N).
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_row(const GemmArgs& p, uint32_t taddr, int row,
+                                             int n0) {
+  constexpr bool DUAL = EPI == kEpiSwiGLU;
+  const int ksplit = p.ksplit;
+  __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    const int col = n0 + c * 32;
+    if (col >= p.N) break;  // warp-uniform
+    if (DUAL) {
+      uint32_t rg[32], ru[32];
+      CFB_TMEM_LD32(taddr + c * 32, rg);
+      CFB_TMEM_LD32(taddr + BN + c * 32, ru);
+      tmem_ld_wait();
+      if (row < p.M) {
+        uint32_t og[16], ou[16], oh[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const float g0 = __uint_as_float(rg[2 * t]) * p.alpha;
+          const float g1 = __uint_as_float(rg[2 * t + 1]) * p.alpha;
+          const float u0 = __uint_as_float(ru[2 * t]) * p.alpha;
+          const float u1 = __uint_as_float(ru[2 * t + 1]) * p.alpha;
+          og[t] = pack_bf16x2(g0, g1);
+          ou[t] = pack_bf16x2(u0, u1);
+          // silu of the bf16-rounded gate, as a separate SwiGLU pass over gu would see it
+          const float2 gr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&og[t]));
+          const float2 ur = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ou[t]));
+          oh[t] = pack_bf16x2(gr.x / (1.f + __expf(-gr.x)) * ur.x,
+                              gr.y / (1.f + __expf(-gr.y)) * ur.y);
+        }
+        __nv_bfloat16* gd = drow + col;
+        __nv_bfloat16* ud = drow + p.dual_off + col;
+        __nv_bfloat16* hd = p.aux + row * p.ld_aux + col;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          reinterpret_cast<uint4*>(gd)[j] = make_uint4(og[4 * j], og[4 * j + 1], og[4 * j + 2], og[4 * j + 3]);
+          reinterpret_cast<uint4*>(ud)[j] = make_uint4(ou[4 * j], ou[4 * j + 1], ou[4 * j + 2], ou[4 * j + 3]);
+          reinterpret_cast<uint4*>(hd)[j] = make_uint4(oh[4 * j], oh[4 * j + 1], oh[4 * j + 2], oh[4 * j + 3]);
+        }
+      }
+      continue;
+    }
+    if (EPI == kEpiBF16Rope && col < p.rope_cols) {
+      // the first-half chunk of a head rotates together with its partner hd/2 columns on
+      const int half = p.hd >> 1;
+      const int hc = col % p.hd;
+      if (hc >= half) continue;  // already written with its partner (warp-uniform)
+      uint32_t ra[32], rb[32];
+      CFB_TMEM_LD32(taddr + c * 32, ra);
+      CFB_TMEM_LD32(taddr + c * 32 + half, rb);
+      tmem_ld_wait();
+      if (row < p.M) {
+        const float4* cs =
+            reinterpret_cast<const float4*>(p.cs + (static_cast<long long>(p.pos[row]) * half + hc) * 2);
+        uint32_t oa[16], ob[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const float4 q = __ldg(cs + t);  // cos, sin of pairs 2t and 2t+1
+          const float a0 = __uint_as_float(ra[2 * t]) * p.alpha;
+          const float a1 = __uint_as_float(ra[2 * t + 1]) * p.alpha;
+          const float b0 = __uint_as_float(rb[2 * t]) * p.alpha;
+          const float b1 = __uint_as_float(rb[2 * t + 1]) * p.alpha;
+          oa[t] = pack_bf16x2(a0 * q.x - b0 * q.y, a1 * q.z - b1 * q.w);
+          ob[t] = pack_bf16x2(b0 * q.x + a0 * q.y, b1 * q.z + a1 * q.w);
+        }
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
+        uint4* da = reinterpret_cast<uint4*>(dst);
+        uint4* db = reinterpret_cast<uint4*>(dst + half);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          da[j] = make_uint4(oa[4 * j], oa[4 * j + 1], oa[4 * j + 2], oa[4 * j + 3]);
+          db[j] = make_uint4(ob[4 * j], ob[4 * j + 1], ob[4 * j + 2], ob[4 * j + 3]);
+        }
+      }
+      continue;
+    }
+    uint32_t r[32];
+    CFB_TMEM_LD32(taddr + c * 32, r);
+    tmem_ld_wait();
+    if (row < p.M) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+      if (EPI == kEpiBF16 || EPI == kEpiBF16Resid || EPI == kEpiBF16Rope) {
+        __nv_bfloat16* dst = drow + col;
+        if (EPI == kEpiBF16Resid) {
+          const uint4* rs = reinterpret_cast<const uint4*>(p.R + row * p.ldr + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 u = rs[j];
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 f = __bfloat1622float2(h[e]);
+              v[j * 8 + 2 * e] += f.x;
+              v[j * 8 + 2 * e + 1] += f.y;
+            }
+          }
+        }
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 u;
+          u.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
+          u.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
+          u.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
+          u.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
+          d4[j] = u;
+        }
+      } else {
+        float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col;
+        float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          if (EPI == kEpiF32Acc && ksplit > 1) {
+            // the k-splits of this tile add into D concurrently (fp32, order not fixed)
+            asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                             d4 + j),
+                         "f"(o.x), "f"(o.y), "f"(o.z), "f"(o.w)
+                         : "memory");
+            continue;
+          }
+          if (EPI == kEpiF32Acc) {
+            const float4 old = d4[j];
+            o.x += old.x;
+            o.y += old.y;
+            o.z += old.z;
+            o.w += old.w;
+          }
+          d4[j] = o;
+        }
+      }
+    }
+  }
+}
+
 // TPM: 0 plain; 1 all-gather consumer (push warps + per-segment waits); 2 reduce-scatter
 // producer (partial rows stored to their owners + sum warps)
 template <int BN, bool A_MN, bool B_MN, int EPI, int TPM = 0>
@@ -365,137 +506,7 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * S::ACC_COLS;
-      __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col = n0 + c * 32;
-        if (col >= p.N) break;  // warp-uniform
-        if (DUAL) {
-          uint32_t rg[32], ru[32];
-          CFB_TMEM_LD32(taddr + c * 32, rg);
-          CFB_TMEM_LD32(taddr + BN + c * 32, ru);
-          tmem_ld_wait();
-          if (row < p.M) {
-            uint32_t og[16], ou[16], oh[16];
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const float g0 = __uint_as_float(rg[2 * t]) * p.alpha;
-              const float g1 = __uint_as_float(rg[2 * t + 1]) * p.alpha;
-              const float u0 = __uint_as_float(ru[2 * t]) * p.alpha;
-              const float u1 = __uint_as_float(ru[2 * t + 1]) * p.alpha;
-              og[t] = pack_bf16x2(g0, g1);
-              ou[t] = pack_bf16x2(u0, u1);
-              // silu of the bf16-rounded gate, as a separate SwiGLU pass over gu would see it
-              const float2 gr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&og[t]));
-              const float2 ur = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ou[t]));
-              oh[t] = pack_bf16x2(gr.x / (1.f + __expf(-gr.x)) * ur.x,
-                                  gr.y / (1.f + __expf(-gr.y)) * ur.y);
-            }
-            __nv_bfloat16* gd = drow + col;
-            __nv_bfloat16* ud = drow + p.dual_off + col;
-            __nv_bfloat16* hd = p.aux + row * p.ld_aux + col;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              reinterpret_cast<uint4*>(gd)[j] = make_uint4(og[4 * j], og[4 * j + 1], og[4 * j + 2], og[4 * j + 3]);
-              reinterpret_cast<uint4*>(ud)[j] = make_uint4(ou[4 * j], ou[4 * j + 1], ou[4 * j + 2], ou[4 * j + 3]);
-              reinterpret_cast<uint4*>(hd)[j] = make_uint4(oh[4 * j], oh[4 * j + 1], oh[4 * j + 2], oh[4 * j + 3]);
-            }
-          }
-          continue;
-        }
-        if (EPI == kEpiBF16Rope && col < p.rope_cols) {
-          // the first-half chunk of a head rotates together with its partner hd/2 columns on
-          const int half = p.hd >> 1;
-          const int hc = col % p.hd;
-          if (hc >= half) continue;  // already written with its partner (warp-uniform)
-          uint32_t ra[32], rb[32];
-          CFB_TMEM_LD32(taddr + c * 32, ra);
-          CFB_TMEM_LD32(taddr + c * 32 + half, rb);
-          tmem_ld_wait();
-          if (row < p.M) {
-            const float4* cs =
-                reinterpret_cast<const float4*>(p.cs + (static_cast<long long>(p.pos[row]) * half + hc) * 2);
-            uint32_t oa[16], ob[16];
-#pragma unroll
-            for (int t = 0; t < 16; ++t) {
-              const float4 q = __ldg(cs + t);  // cos, sin of pairs 2t and 2t+1
-              const float a0 = __uint_as_float(ra[2 * t]) * p.alpha;
-              const float a1 = __uint_as_float(ra[2 * t + 1]) * p.alpha;
-              const float b0 = __uint_as_float(rb[2 * t]) * p.alpha;
-              const float b1 = __uint_as_float(rb[2 * t + 1]) * p.alpha;
-              oa[t] = pack_bf16x2(a0 * q.x - b0 * q.y, a1 * q.z - b1 * q.w);
-              ob[t] = pack_bf16x2(b0 * q.x + a0 * q.y, b1 * q.z + a1 * q.w);
-            }
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col;
-            uint4* da = reinterpret_cast<uint4*>(dst);
-            uint4* db = reinterpret_cast<uint4*>(dst + half);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              da[j] = make_uint4(oa[4 * j], oa[4 * j + 1], oa[4 * j + 2], oa[4 * j + 3]);
-              db[j] = make_uint4(ob[4 * j], ob[4 * j + 1], ob[4 * j + 2], ob[4 * j + 3]);
-            }
-          }
-          continue;
-        }
-        uint32_t r[32];
-        CFB_TMEM_LD32(taddr + c * 32, r);
-        tmem_ld_wait();
-        if (row < p.M) {
-          float v[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
-          if (EPI == kEpiBF16 || EPI == kEpiBF16Resid || EPI == kEpiBF16Rope) {
-            __nv_bfloat16* dst = drow + col;
-            if (EPI == kEpiBF16Resid) {
-              const uint4* rs = reinterpret_cast<const uint4*>(p.R + row * p.ldr + col);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint4 u = rs[j];
-                const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  float2 f = __bfloat1622float2(h[e]);
-                  v[j * 8 + 2 * e] += f.x;
-                  v[j * 8 + 2 * e + 1] += f.y;
-                }
-              }
-            }
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              uint4 u;
-              u.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
-              u.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
-              u.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
-              u.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
-              d4[j] = u;
-            }
-          } else {
-            float* dst = reinterpret_cast<float*>(p.D) + row * p.ldd + col;
-            float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-              if (EPI == kEpiF32Acc && ksplit > 1) {
-                // the k-splits of this tile add into D concurrently (fp32, order not fixed)
-                asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
-                                 d4 + j),
-                             "f"(o.x), "f"(o.y), "f"(o.z), "f"(o.w)
-                             : "memory");
-                continue;
-              }
-              if (EPI == kEpiF32Acc) {
-                const float4 old = d4[j];
-                o.x += old.x;
-                o.y += old.y;
-                o.z += old.z;
-                o.w += old.w;
-              }
-              d4[j] = o;
-            }
-          }
-        }
-      }
+      epilogue_row<BN, EPI>(p, taddr, row, n0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&tempty[acc]));
@@ -666,6 +677,218 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM
+// Two CTAs of a cluster (one per SM) compute a 256 x 256 tile with tcgen05.mma.cta_group::2.
+// Per k-block each CTA stages its 128 rows of A and 128 of the 256 B columns (32 KB, where a
+// single CTA computing a 128 x 256 tile stages 48 KB), so the L2 -> shared-memory traffic per
+// FLOP drops by a third and the ring is 6 stages deep.  Roles as in the single-CTA kernel.
+// The leader (cluster rank 0) issues the MMAs and owns the full and accumulator-empty
+// barriers: both CTAs' TMA copies count their bytes on the leader's full barrier and both
+// CTAs' epilogue warps arrive on its accumulator-empty barrier; MMA completion is signalled to
+// the same barrier offsets of both CTAs.  Each CTA's TMEM holds the fp32 accumulators of its
+// 128 rows (2 x 256 columns), which its own epilogue warps drain.  Plain GEMMs only (no
+// tensor-parallel modes, no dual-B); split-K as in the single-CTA kernel.
+struct PairShape {
+  static constexpr int BM = 128;  // rows per CTA; the pair tile is 256 rows
+  static constexpr int BN = 256;  // pair tile columns; each CTA stages BN / 2 rows of B
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 6;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int ACC_COLS = BN;
+  static constexpr int TMEM_COLS = 512;
+};
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tmA,
+                         const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+  using S = PairShape;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* bar_area = smem + S::STAGES * S::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(bar_area);
+  uint64_t* empty = full + S::STAGES;
+  uint64_t* tfull = empty + S::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (p.M + 2 * S::BM - 1) / (2 * S::BM);
+  const int num_n = (p.N + S::BN - 1) / S::BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + S::BK - 1) / S::BK;
+  const int ksplit = p.ksplit;
+  const int num_units = num_tiles * ksplit;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&tfull[a]), 1);
+      mbar_init(smem_u32(&tempty[a]), 8);  // 4 epilogue warps of each CTA
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t smem_base = smem_u32(smem);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (both CTAs)
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int unit = pair; unit < num_units && ok; unit += num_pairs) {
+        const int tile = unit / ksplit, ks = unit - tile * ksplit;
+        int tm, tn;
+        tile_coords(tile, num_m, num_n, tm, tn);
+        const int m0 = tm * 2 * S::BM + static_cast<int>(crank) * S::BM;
+        const int nb0 = tn * S::BN + static_cast<int>(crank) * (S::BN / 2);
+        const int kb_end = (ks + 1) * num_kb / ksplit;
+        for (int kb = ks * num_kb / ksplit; kb < kb_end; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err,
+                         kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&full[stage]);
+          if (leader) mbar_arrive_expect_tx(fb, 2 * S::STAGE_BYTES);
+          const uint32_t fb_leader = mapa_shared(fb, 0);
+          const uint32_t sa = smem_base + stage * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+          const int k0 = kb * S::BK;
+          if (!A_MN) {
+            tma_load_2d_pair(sa, &tmA, fb_leader, k0, m0);
+          } else {
+            tma_load_2d_pair(sa, &tmA, fb_leader, m0, k0);
+            tma_load_2d_pair(sa + 8192, &tmA, fb_leader, m0 + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(sb, &tmB, fb_leader, k0, nb0);
+          } else {
+            tma_load_2d_pair(sb, &tmB, fb_leader, nb0, k0);
+            tma_load_2d_pair(sb + 8192, &tmB, fb_leader, nb0 + 64, k0);
+          }
+          ++issued;
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // On the error path let the copies land before the CTA exits (bounded); only the leader
+      // can wait on the barrier they count on.
+      if (!ok && leader) tma_drain_ring(full, S::STAGES, issued);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer (leader)
+      constexpr uint32_t IDESC = idesc_bf16_f32(2 * S::BM, S::BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int unit = pair; unit < num_units && ok; unit += num_pairs, ++it) {
+        const int ks = unit % ksplit;
+        const int kb_beg = ks * num_kb / ksplit, kb_end = (ks + 1) * num_kb / ksplit;
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(smem_u32(&tempty[acc]), acc_phase ^ 1u, abort_flag, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
+        for (int kb = kb_beg; kb < kb_end; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < S::BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(sa + k * 2048, 8192, 1024)
+                                     : sdesc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(sb + k * 2048, 8192, 1024)
+                                     : sdesc_sw128(sb + k * 32, 16, 1024);
+            umma_bf16_ss_pair(d_tmem, ad, bd, IDESC, (kb != kb_beg || k != 0) ? 1u : 0u);
+          }
+          umma_commit_pair_mc(smem_u32(&empty[stage]), 0x3);
+          if (++stage == S::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(smem_u32(&tfull[acc]), 0x3);
+      }
+      // All issued MMAs complete (they read both CTAs' shared memory) before either CTA moves on.
+      umma_commit_pair(smem_u32(drain));
+      volatile int dummy = 0;
+      mbar_wait(smem_u32(drain), 0, &dummy, nullptr, 0);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (warps 2..5)
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    int it = 0;
+    for (int unit = pair; unit < num_units; unit += num_pairs, ++it) {
+      const int tile = unit / ksplit;
+      int tm, tn;
+      tile_coords(tile, num_m, num_n, tm, tn);
+      const int m0 = tm * 2 * S::BM + static_cast<int>(crank) * S::BM, n0 = tn * S::BN;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err, kErrWaitEpilogue))
+        break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * S::ACC_COLS;
+      epilogue_row<S::BN, EPI>(p, taddr, m0 + row_in_tile, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // the leader's MMAs no longer read this CTA's shared memory
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -765,42 +988,114 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
   return -4;
 }
 
+template <bool A_MN, bool B_MN, int EPI>
+static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                            cudaStream_t st) {
+  using S = PairShape;
+  auto kern = gemm_bf16_sm100_pair<A_MN, B_MN, EPI>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  static int max_pairs = 0;
+  if (max_pairs == 0) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    max_pairs = n < num_sms() / 2 ? n : num_sms() / 2;
+  }
+  const long long units =
+      static_cast<long long>((a.M + 255) / 256) * ((a.N + 255) / 256) * a.ksplit;
+  const int pairs = units < max_pairs ? static_cast<int>(units) : max_pairs;
+  cfg.gridDim = dim3(2 * pairs);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
+  return e == cudaSuccess ? 0 : -3;
+}
+
+template <int EPI>
+static int dispatch_pair_major(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                               const GemmArgs& a, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_gemm_pair<false, false, EPI>(ta, tb, a, st);
+  if (!a_mn && b_mn) return launch_gemm_pair<false, true, EPI>(ta, tb, a, st);
+  if (a_mn && b_mn) return launch_gemm_pair<true, true, EPI>(ta, tb, a, st);
+  return launch_gemm_pair<true, false, EPI>(ta, tb, a, st);
+}
+
+static int dispatch_pair(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
+                         const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+  switch (epi) {
+    case kEpiBF16: return dispatch_pair_major<kEpiBF16>(a_mn, b_mn, ta, tb, a, st);
+    case kEpiBF16Resid: return dispatch_pair_major<kEpiBF16Resid>(a_mn, b_mn, ta, tb, a, st);
+    case kEpiF32: return dispatch_pair_major<kEpiF32>(a_mn, b_mn, ta, tb, a, st);
+    case kEpiF32Acc: return dispatch_pair_major<kEpiF32Acc>(a_mn, b_mn, ta, tb, a, st);
+    case kEpiBF16Rope:
+      if (a_mn || b_mn) return -4;
+      return launch_gemm_pair<false, false, kEpiBF16Rope>(ta, tb, a, st);
+  }
+  return -4;
+}
+
 }  // namespace cfb
 
 using namespace cfb;
 
-// Tile width and split-K factor of a weight-gradient GEMM (fp32 accumulate into D).  The K
-// (token) dimension is long and M x N (the weight) often yields a tile count just above a
-// multiple of the SM count, leaving most SMs idle in the last wave; splitting K into s ranges
-// multiplies the work units by s.  Picks the (bn, s) with the best wave efficiency
-// units / (waves * SMs), s <= 4 and at least 16 k-blocks of 64 per unit, preferring bn = 256
-// (less L2 -> smem traffic per FLOP) and the smallest s within 0.03 of the best.
-static void choose_split_k(int M, int N, int K, int& bn, int& ksplit) {
+// Tile shape and split-K factor of a GEMM.  Candidates: a 256 x 256 tile on a CTA pair
+// (`pair`), or a 128 x bn tile on one CTA (bn = 128 or 256); with `can_split` (fp32 accumulate
+// epilogue) each tile may also be split into s <= 4 ranges of at least 16 k-blocks, whose
+// partial sums are reduced into D.  The estimated time of a candidate is
+//   waves * (k-blocks per unit) * (SM time per k-block)
+// with waves = ceil(units / slots) (slots: SMs, or co-resident CTA pairs), and the SM time per
+// k-block of a 128 x 256 share measured relative to the single-CTA bn = 256 kernel: the bn = 128
+// kernel moves 4/3 as many operand bytes per FLOP and runs about 1/3 slower, the pair kernel
+// moves 2/3 as many.  Splits pay 2% each for their fp32 reduction traffic.  A later candidate
+// must win by 3% (the pair kernel without split is tried first).
+struct GemmPlan {
+  int bn;
+  int ksplit;
+  bool pair;
+};
+
+// bn_req: 0 any tile, 128 / 256 that single-CTA tile only, -1 the pair tile only
+static GemmPlan plan_gemm(int M, int N, int K, int bn_req, bool can_split, bool can_pair) {
   const int sms = num_sms();
   const int num_kb = (K + 63) / 64;
-  const int bns[2] = {256, 128};
-  double best = -1.0;
-  int best_bn = 256, best_s = 1;
-  for (int b : bns) {
-    if ((bn == 128 || bn == 256) && b != bn) continue;
-    if (b == 256 && N <= 128) continue;
-    const long long tiles = ((M + 127LL) / 128) * ((N + b - 1LL) / b);
-    for (int s = 1; s <= 4; ++s) {
-      if (s > 1 && num_kb / s < 16) break;
-      const long long units = tiles * s;
-      const long long waves = (units + sms - 1) / sms;
-      double eff = static_cast<double>(units) / static_cast<double>(waves * sms);
-      if (b == 128) eff -= 0.05;  // more operand traffic per FLOP than bn = 256
-      eff -= 0.01 * (s - 1);      // fp32 reduction traffic of the extra splits
-      if (eff > best + 0.03) {
-        best = eff;
-        best_bn = b;
-        best_s = s;
-      }
+  GemmPlan best{256, 1, false};
+  double best_t = 1e300;
+  auto consider = [&](int bn, bool pair, int s) {
+    if (s > 1 && num_kb / s < 16) return;
+    const long long tiles = pair ? ((M + 255LL) / 256) * ((N + 255LL) / 256)
+                                 : ((M + 127LL) / 128) * ((N + bn - 1LL) / bn);
+    const long long units = tiles * s;
+    const int slots = pair ? sms / 2 : sms;
+    const long long waves = (units + slots - 1) / slots;
+    const double kbpu = static_cast<double>((num_kb + s - 1) / s);
+    const double per_kb = pair ? 0.9 : (bn == 256 ? 1.0 : 0.5 * 1.33);
+    double t = static_cast<double>(waves) * kbpu * per_kb * (1.0 + 0.02 * (s - 1));
+    if (t < best_t * 0.97) {
+      best_t = t;
+      best = GemmPlan{pair ? 256 : bn, s, pair};
     }
+  };
+  const int max_s = can_split ? 4 : 1;
+  const bool single256 = bn_req == 256 || (bn_req == 0 && N > 128);
+  const bool single128 = bn_req == 128 || bn_req == 0;
+  for (int s = 1; s <= max_s; ++s) {
+    if (can_pair) consider(256, true, s);
+    if (single256) consider(256, false, s);
+    if (single128) consider(128, false, s);
   }
-  bn = best_bn;
-  ksplit = best_s;
+  return best;
 }
 
 static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, long long ldb,
@@ -813,14 +1108,26 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (reinterpret_cast<uintptr_t>(D) & 15))
     return -12;
-  int ksplit = 1;
-  // CFB_GEMM_SPLIT_K=0 keeps one unit per tile (fixed fp32 summation order)
+  // CFB_GEMM_SPLIT_K=0 keeps one unit per tile (fixed fp32 summation order);
+  // CFB_GEMM_PAIR=0 keeps every GEMM on single-CTA tiles
   static const bool split_k_on = [] {
     const char* e = std::getenv("CFB_GEMM_SPLIT_K");
     return !(e && e[0] == '0');
   }();
-  if (epi == kEpiF32Acc && !tp && max_ctas <= 0 && (ldd % 4) == 0 && split_k_on) {
-    choose_split_k(M, N, K, bn, ksplit);
+  static const bool pair_on = [] {
+    const char* e = std::getenv("CFB_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  int ksplit = 1;
+  bool pair = false;
+  if (!tp && max_ctas <= 0 && epi != kEpiSwiGLU) {
+    const bool can_split = epi == kEpiF32Acc && (ldd % 4) == 0 && split_k_on;
+    const bool force_pair = bn == kGemmTilePair;
+    const bool can_pair = force_pair || (pair_on && bn == 0);
+    const GemmPlan pl = plan_gemm(M, N, K, force_pair ? -1 : bn, can_split, can_pair);
+    bn = pl.bn;
+    ksplit = pl.ksplit;
+    pair = pl.pair;
   } else if (bn != 128 && bn != 256) {
     const long long tiles256 = ((M + 127LL) / 128) * ((N + 255LL) / 256);
     bn = (N <= 128 || tiles256 < num_sms()) ? 128 : 256;
@@ -832,7 +1139,7 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
             : make_tmap_2d_bf16(&ta, A, M, K, lda, 64, 128);
   if (rc) return rc * 100 - 1;
   rc = b_mn ? make_tmap_2d_bf16(&tb, B, K, N, ldb, 64, 64)
-            : make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, bn);
+            : make_tmap_2d_bf16(&tb, B, N, K, ldb, 64, pair ? 128 : bn);
   if (rc) return rc * 100 - 2;
   GemmArgs a;
   a.M = M;
@@ -916,6 +1223,7 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
     return bn == 256 ? CFB_TP2(256, false) : CFB_TP2(128, false);
 #undef CFB_TP2
   }
+  if (pair) return dispatch_pair(epi, a_mn, b_mn, ta, tb, a, st);
   if (bn == 256) return dispatch_epi<256>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
   return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
 }

@@ -7,6 +7,9 @@
 #include <stdint.h>
 
 enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3, kEpiBF16Rope = 4, kEpiSwiGLU = 5 };
+// `bn` value of cfb_gemm_bf16 that selects the 256 x 256 tile on a CTA pair (cta_group::2);
+// 128 / 256 select a single-CTA tile of that width, 0 lets the planner choose
+enum { kGemmTilePair = 512 };
 
 // GEMM (gemm_sm100.cu): D = alpha * op(A) op(B) with the epilogue `epi`.
 int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,

@@ -34,8 +34,24 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, a_mn: bool, b_mn: 
         else:
             out.copy_(r)
         return out
+    _check_gemm_operands(a, b, out, b_mn)
     kernels().gemm(a, b, out, a_mn, b_mn, epi, resid, alpha, bn, max_ctas)
     return out
+
+
+def _check_gemm_operands(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, b_mn: bool):
+    """Shape and alignment rules of the tcgen05 GEMM (TMA rows start on 16 bytes, the epilogue
+    stores 32-column chunks), checked before the launch so a bad call raises here."""
+    N = b.shape[1] if b_mn else b.shape[0]
+    if N % 32:
+        raise ValueError(f"gemm: N = {N} is not a multiple of 32")
+    for name, t in (("a", a), ("b", b), ("out", out)):
+        if t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"gemm: {name} must be 2-D with unit column stride")
+        if t.data_ptr() % 16:
+            raise ValueError(f"gemm: {name} is not 16-byte aligned")
+    if a.stride(0) % 8 or b.stride(0) % 8:
+        raise ValueError("gemm: row strides of a and b must be multiples of 8 elements")
 
 
 def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,

@@ -18,7 +18,7 @@ def rel_err(a, b):
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (304, 512, 200), (1024, 2560, 2048),
                                    (80, 96, 136)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 256, 512])  # 512: 256 x 256 tile on a CTA pair
 def test_gemm_layouts(M, N, K, a_mn, b_mn, bn):
     torch.manual_seed(0)
     A = torch.randn(M, K, device=dev).bfloat16()
@@ -34,9 +34,9 @@ def test_gemm_layouts(M, N, K, a_mn, b_mn, bn):
     assert kernels().gemm_error_word(0, True) == 0
 
 
-def test_gemm_epilogues():
+@pytest.mark.parametrize("M,N,K", [(512, 768, 384), (4096, 2048, 1024), (300, 1000 - 8, 544)])
+def test_gemm_epilogues(M, N, K):
     torch.manual_seed(1)
-    M, N, K = 512, 768, 384
     x = torch.randn(M, K, device=dev).bfloat16()
     w = torch.randn(N, K, device=dev).bfloat16()
     r = torch.randn(M, N, device=dev).bfloat16()
@@ -50,6 +50,15 @@ def test_gemm_epilogues():
     assert rel_err(dw, 1 + dy.float().t() @ x.float()) < 1e-2
     gemm.linear_wgrad(dy, x, dw, accumulate=False, alpha=0.5)
     assert rel_err(dw, 0.5 * dy.float().t() @ x.float()) < 1e-2
+
+
+def test_gemm_rejects_unsupported_shapes():
+    x = torch.randn(64, 520, device=dev).bfloat16()
+    w = torch.randn(96, 520, device=dev).bfloat16()
+    with pytest.raises(ValueError):
+        gemm.linear_dgrad(torch.randn(64, 96, device=dev).bfloat16(), w)  # N = 520
+    with pytest.raises(ValueError):
+        gemm.linear_fwd(x[:, 1:513], w[:, :512])  # a not 16-byte aligned
 
 
 @pytest.mark.parametrize("M,N,K", [(2560, 2048, 8192), (2048, 5632, 4096), (768, 4096, 6000)])
@@ -231,7 +240,8 @@ def test_gemm_swiglu_epilogue(M, F, K):
 
 
 @pytest.mark.parametrize("M,nh,nkv,hd,bn", [(4096, 32, 4, 64, 0), (1000, 8, 2, 128, 128),
-                                            (333, 4, 4, 64, 256), (2048, 16, 8, 128, 256)])
+                                            (333, 4, 4, 64, 256), (2048, 16, 8, 128, 256),
+                                            (1000, 8, 2, 128, 512), (2048, 16, 8, 64, 512)])
 def test_gemm_rope_epilogue(M, nh, nkv, hd, bn):
     """QKV projection with RoPE in the epilogue vs the fp32 projection followed by RoPE."""
     from centrifuge_b200.ops import kernels
