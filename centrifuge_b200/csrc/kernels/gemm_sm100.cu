@@ -686,8 +686,11 @@ __global__ void __launch_bounds__(TPM != 0 ? 256 : 192, 1)
 // barriers: both CTAs' TMA copies count their bytes on the leader's full barrier and both
 // CTAs' epilogue warps arrive on its accumulator-empty barrier; MMA completion is signalled to
 // the same barrier offsets of both CTAs.  Each CTA's TMEM holds the fp32 accumulators of its
-// 128 rows (2 x 256 columns), which its own epilogue warps drain.  Plain GEMMs only (no
-// tensor-parallel modes, no dual-B); split-K as in the single-CTA kernel.
+// 128 rows (2 x 256 columns), which its own epilogue warps drain.  No tensor-parallel modes;
+// split-K as in the single-CTA kernel.  SwiGLU (dual-B): the leader stages 128 gate rows of B
+// and its peer the 128 matching up rows (dual_off further down), so one N = 256 MMA leaves gate
+// in accumulator columns [0, 128) and up in [128, 256) of every row, and a tile covers 128
+// output columns of F.
 struct PairShape {
   static constexpr int BM = 128;  // rows per CTA; the pair tile is 256 rows
   static constexpr int BN = 256;  // pair tile columns; each CTA stages BN / 2 rows of B
@@ -706,6 +709,8 @@ __global__ void __launch_bounds__(192, 1)
     gemm_bf16_sm100_pair(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
   using S = PairShape;
+  constexpr bool DUAL = EPI == kEpiSwiGLU;
+  constexpr int TN = DUAL ? S::BN / 2 : S::BN;  // output columns of a tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -725,7 +730,7 @@ __global__ void __launch_bounds__(192, 1)
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   const int num_m = (p.M + 2 * S::BM - 1) / (2 * S::BM);
-  const int num_n = (p.N + S::BN - 1) / S::BN;
+  const int num_n = (p.N + TN - 1) / TN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + S::BK - 1) / S::BK;
   const int ksplit = p.ksplit;
@@ -770,7 +775,8 @@ __global__ void __launch_bounds__(192, 1)
         int tm, tn;
         tile_coords(tile, num_m, num_n, tm, tn);
         const int m0 = tm * 2 * S::BM + static_cast<int>(crank) * S::BM;
-        const int nb0 = tn * S::BN + static_cast<int>(crank) * (S::BN / 2);
+        const int nb0 = DUAL ? tn * TN + (crank ? p.dual_off : 0)
+                             : tn * S::BN + static_cast<int>(crank) * (S::BN / 2);
         const int kb_end = (ks + 1) * num_kb / ksplit;
         for (int kb = ks * num_kb / ksplit; kb < kb_end; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1u, abort_flag, p.err,
@@ -866,14 +872,14 @@ __global__ void __launch_bounds__(192, 1)
       const int tile = unit / ksplit;
       int tm, tn;
       tile_coords(tile, num_m, num_n, tm, tn);
-      const int m0 = tm * 2 * S::BM + static_cast<int>(crank) * S::BM, n0 = tn * S::BN;
+      const int m0 = tm * 2 * S::BM + static_cast<int>(crank) * S::BM, n0 = tn * TN;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(smem_u32(&tfull[acc]), acc_phase, abort_flag, p.err, kErrWaitEpilogue))
         break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * S::ACC_COLS;
-      epilogue_row<S::BN, EPI>(p, taddr, m0 + row_in_tile, n0);
+      epilogue_row<TN, EPI>(p, taddr, m0 + row_in_tile, n0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
@@ -1015,8 +1021,9 @@ static int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const 
     }
     max_pairs = n < num_sms() / 2 ? n : num_sms() / 2;
   }
+  constexpr int TN = EPI == kEpiSwiGLU ? 128 : 256;
   const long long units =
-      static_cast<long long>((a.M + 255) / 256) * ((a.N + 255) / 256) * a.ksplit;
+      static_cast<long long>((a.M + 255) / 256) * ((a.N + TN - 1) / TN) * a.ksplit;
   const int pairs = units < max_pairs ? static_cast<int>(units) : max_pairs;
   cfg.gridDim = dim3(2 * pairs);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, a);
@@ -1273,6 +1280,11 @@ int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, 
   a.aux = static_cast<__nv_bfloat16*>(Hout);
   a.ld_aux = ld_h;
   a.P = 1;
+  static const bool pair_on = [] {
+    const char* e = std::getenv("CFB_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  if (pair_on) return launch_gemm_pair<false, false, kEpiSwiGLU>(ta, tb, a, st);
   return launch_gemm<128, false, false, kEpiSwiGLU>(ta, tb, a, st, 0);
 }
 
