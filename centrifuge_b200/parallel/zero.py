@@ -10,10 +10,14 @@ range is cut into buckets; rank ``r`` owns chunk ``r`` of every bucket ("bucket-
 sharding), so a bucket is reduce-scattered as soon as the backward has finished it and each
 rank's optimizer shard is the concatenation of its chunks.
 
-Per micro-batch (stage 2): when a bucket's gradients are final the bucket is reduced on a
-communication stream into the rank's fp32 gradient shard (accumulating over micro-batches) and
-its slice of the local gradient buffer is cleared for the next micro-batch.  Stage 1 accumulates
-the full local gradients over the micro-batches and reduces once at the boundary.
+Stage 2: when a bucket's gradients are final the bucket is reduced on a communication stream
+into the rank's fp32 gradient shard and its slice of the local gradient buffer is cleared.  By
+default this happens only in the backward of the last micro-batch of a step: the earlier
+micro-batches accumulate into the local fp32 buffer (which is full-size here anyway), so a step
+moves each gradient over NVLink once instead of ``grad_accum`` times, and the reduction still
+overlaps the last backward bucket by bucket.  ``reduce_every_micro=True`` reduces in every
+micro-batch's backward, as DeepSpeed's ZeRO-2 does.  Stage 1 accumulates the full local
+gradients over the micro-batches and reduces once at the boundary, without overlap.
 
 Step: global grad-norm (local sum of squares + one 4-byte all-reduce), clip coefficient computed
 on the device, fused AdamW on the fp32 master shard writing bf16 parameters, then a per-bucket
@@ -95,8 +99,10 @@ class ZeroAdamW:
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0,
                  grad_clip: float = 1.0, bucket_numel: int = 1 << 26, reducer=None,
                  overlap: bool = True, norm_group=None, replicated_ranges=(),
-                 replication: Optional[int] = None):
+                 replication: Optional[int] = None, reduce_every_micro: bool = False):
         assert stage in (1, 2)
+        self.reduce_every_micro = reduce_every_micro
+        self._active = True  # this micro-batch's backward reduces buckets
         self.flat = flat
         self.group = group
         self.stage = stage
@@ -163,10 +169,14 @@ class ZeroAdamW:
         if self.stage == 2 and self.W > 1:
             model.grad_ready_hook = self.on_grads_ready
 
-    def begin_micro(self) -> None:
+    def begin_micro(self, last: bool = True) -> None:
+        """Start a micro-batch; ``last`` marks the last one before :meth:`step`."""
         self._ready = 0
+        self._active = last or self.reduce_every_micro
 
     def on_grads_ready(self, lo: int, hi: int) -> None:
+        if not self._active:
+            return  # gradients keep accumulating in the local buffer
         # gradients complete front to back: every bucket ending at or before `hi` is final
         while self._ready < len(self.buckets) and self.buckets[self._ready].hi <= hi:
             self._reduce_bucket(self.buckets[self._ready])
@@ -186,7 +196,7 @@ class ZeroAdamW:
 
     def end_micro(self) -> None:
         """Finish the micro-batch: reduce what is left (stage 2) and join the comm stream."""
-        if self.W == 1:
+        if self.W == 1 or not self._active:
             return
         if self.stage == 2:
             self.on_grads_ready(0, self.flat.numel)

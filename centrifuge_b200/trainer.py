@@ -34,7 +34,9 @@ class Trainer:
         if hasattr(optimizer, "attach"):
             optimizer.attach(model)
 
-    def micro_step(self, batch: Batch) -> torch.Tensor:
+    def micro_step(self, batch: Batch, last: bool = True) -> torch.Tensor:
+        """Forward + filtered backward of one micro-batch; ``last`` marks the last micro-batch
+        before the optimizer step (the data-parallel gradient reduction runs in its backward)."""
         ids = batch.input_ids
         B, S = ids.shape
         out = self.model(ids)
@@ -52,7 +54,7 @@ class Trainer:
             loss = token_filter_loss(ids, None, mask, None, None, None, True,
                                      per_token_loss=out.token_loss)
         if hasattr(self.opt, "begin_micro"):
-            self.opt.begin_micro()
+            self.opt.begin_micro(last=last)
         loss.backward()
         if hasattr(self.opt, "end_micro"):
             self.opt.end_micro()
@@ -62,10 +64,10 @@ class Trainer:
         """One optimizer step over ``grad_accum`` micro-batches; returns the mean loss (device)."""
         assert len(batches) == self.grad_accum
         total = torch.zeros((), device=self.device)
-        for b in batches:
+        for i, b in enumerate(batches):
             if to_device:
                 b = b.to(self.device, non_blocking=True)
-            total += self.micro_step(b)
+            total += self.micro_step(b, last=(i == len(batches) - 1))
         self.opt.step(grad_scale=1.0 / (self.grad_accum * self.world))
         self.opt.zero_grad()
         return total / self.grad_accum

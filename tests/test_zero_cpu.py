@@ -33,7 +33,7 @@ def _batches(cfg, n, B=2, S=40):
     return out
 
 
-def _train(rank, world, stage, ga, steps, tmpdir):
+def _train(rank, world, stage, ga, steps, tmpdir, every=False):
     import os
 
     import torch.distributed as dist
@@ -45,7 +45,7 @@ def _train(rank, world, stage, ga, steps, tmpdir):
     group = dist.group.WORLD if world > 1 else None
     red = NcclReducer(group, comm_dtype=torch.float32) if world > 1 else None
     opt = ZeroAdamW(model.flat, group=group, stage=stage, lr=1e-3, grad_clip=1.0,
-                    bucket_numel=4096, reducer=red)
+                    bucket_numel=4096, reducer=red, reduce_every_micro=every)
     tr = Trainer(model, opt, drop_rate=0.5, grad_accum=ga, world_size=world)
     allb = _batches(cfg, steps * ga * world)
     for s in range(steps):
@@ -55,10 +55,11 @@ def _train(rank, world, stage, ga, steps, tmpdir):
     return model.flat.data.numpy().copy(), float(opt._norm.item())
 
 
-@pytest.mark.parametrize("stage", [1, 2])
-def test_zero_matches_single_rank(stage, tmp_path):
+@pytest.mark.parametrize("stage,every", [(1, False), (2, False), (2, True)])
+def test_zero_matches_single_rank(stage, every, tmp_path):
+    """Stage 2 reduces in the last micro-batch's backward (default) or in every one."""
     world, ga, steps = 2, 2, 2
-    multi = run_ranks(_train, world, stage, ga, steps, str(tmp_path))
+    multi = run_ranks(_train, world, stage, ga, steps, str(tmp_path), every)
     single = _train(0, 1, stage, ga * world, steps, str(tmp_path))
     for r in range(world):
         p, norm = multi[r]
