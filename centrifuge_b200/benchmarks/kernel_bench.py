@@ -78,6 +78,39 @@ def bench_gemm(shapes, bn=0, cublas=True, compare=False):
     return rows
 
 
+def bench_fusions(T=16384, Tk=8192, H=2048, F=5632):
+    """GEMMs with fused epilogues against the same GEMM followed by the separate kernel, at the
+    TinyLlama MLP shapes (T tokens forward, Tk kept rows backward); times back to back."""
+    from centrifuge_b200.ops import fused
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    wgu = (torch.randn(2 * F, H, device="cuda") / H ** 0.5).bfloat16()
+    wd = (torch.randn(H, F, device="cuda") / F ** 0.5).bfloat16()
+    dy = torch.randn(Tk, H, device="cuda").bfloat16()
+    rows = torch.randperm(T, device="cuda")[:Tk].sort().values.int()
+    gu, _ = gemm.linear_fwd_swiglu(x, wgu)
+    res = []
+
+    def unfused_fwd():
+        g = gemm.linear_fwd(x, wgu)
+        return fused.swiglu_fwd(g)
+
+    def unfused_bwd():
+        dh = gemm.linear_dgrad(dy, wd)
+        return fused.swiglu_bwd(dh, gu, rows)
+
+    for name, f_fused, f_sep, fl in (
+            ("swiglu_fwd_gemm", lambda: gemm.linear_fwd_swiglu(x, wgu), unfused_fwd,
+             2.0 * T * H * 2 * F),
+            ("swiglu_bwd_gemm", lambda: gemm.linear_dgrad_swiglu(dy, wd, gu, rows), unfused_bwd,
+             2.0 * Tk * H * F)):
+        t_f = _time(f_fused)
+        t_s = _time(f_sep)
+        res.append({"name": name, "fused_ms": t_f, "separate_ms": t_s,
+                    "fused_tflops": fl / t_f / 1e9, "separate_tflops": fl / t_s / 1e9})
+        print(json.dumps(res[-1]))
+    return res
+
+
 def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3)):
     ld = (nh + 2 * nkv) * hd
     qkv = torch.randn(B * S, ld, device="cuda").bfloat16()
@@ -131,6 +164,8 @@ def main():
     ap.add_argument("--json", default=None)
     ap.add_argument("--skip-attn", action="store_true")
     ap.add_argument("--skip-gemm", action="store_true")
+    ap.add_argument("--fusions", action="store_true",
+                    help="fused-epilogue GEMMs vs GEMM + separate kernel (MLP shapes)")
     ap.add_argument("--attn-shape", default="4,4096,32,8,128",
                     help="B,S,nh,nkv,hd of the attention benchmark")
     ap.add_argument("--shapes", default=None, help="comma-separated GEMM shape names")
@@ -164,6 +199,8 @@ def main():
     if not args.skip_gemm:
         out["gemm"] = bench_gemm(shapes, bn=args.bn, cublas=not args.no_cublas,
                                  compare=args.compare_tiles)
+    if args.fusions:
+        out["fusions"] = bench_fusions()
     if not args.skip_attn:
         B, S, nh, nkv, hd = (int(x) for x in args.attn_shape.split(","))
         keeps = tuple(float(x) for x in args.keeps.split(","))

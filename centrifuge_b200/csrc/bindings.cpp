@@ -140,6 +140,37 @@ void gemm_swiglu(const Tensor& x, const Tensor& w, Tensor& gu, Tensor& h) {
                "gemm_swiglu");
 }
 
+// dgu [M, 2F] = SwiGLU backward of dh = dy @ wd (wd [H, F], read MN-major) with the gate/up
+// activations of row gu_rows[m] (or m) of gu [*, 2F]; dh stays in TMEM.
+void gemm_swiglu_bwd(const Tensor& dy, const Tensor& wd, const Tensor& gu,
+                     const c10::optional<Tensor>& gu_rows, Tensor& dgu) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(wd, "wd");
+  check_bf16_2d(gu, "gu");
+  check_bf16_2d(dgu, "dgu");
+  const int64_t M = dy.size(0), K = dy.size(1), F = wd.size(1);
+  TORCH_CHECK(wd.size(0) == K, "gemm_swiglu_bwd: wd must be [H, F] with H = dy.size(1)");
+  TORCH_CHECK(gu.size(1) == 2 * F && dgu.size(0) == M && dgu.size(1) == 2 * F,
+              "gemm_swiglu_bwd: gu / dgu must have 2F columns");
+  const int* rows = nullptr;
+  if (gu_rows.has_value() && gu_rows->defined()) {
+    TORCH_CHECK(gu_rows->is_cuda() && gu_rows->scalar_type() == at::kInt &&
+                    gu_rows->numel() == M && gu_rows->is_contiguous(),
+                "gemm_swiglu_bwd: gu_rows must be int32 [M] on the device");
+    rows = gu_rows->data_ptr<int>();
+  } else {
+    TORCH_CHECK(gu.size(0) == M, "gemm_swiglu_bwd: gu must have M rows without gu_rows");
+  }
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(dy.device());
+  CFB_CHECK_RC(cfb_gemm_swiglu_bwd(dy.data_ptr(), dy.stride(0), wd.data_ptr(), wd.stride(0),
+                                   gu.data_ptr(), gu.stride(0), rows, dgu.data_ptr(),
+                                   dgu.stride(0), static_cast<int>(M), static_cast<int>(F),
+                                   static_cast<int>(K), err_word(dy.get_device()).data_ptr<int>(),
+                                   cur_stream()),
+               "gemm_swiglu_bwd");
+}
+
 // ---- tensor-parallel fusion (pointers into symmetric memory are raw device addresses)
 // out = a @ b^T (a @ b with b_mn) fused with a sequence-parallel collective over NVLink:
 // mode 1 all-gathers this rank's rows of `a` to every rank while computing, mode 2 writes the
@@ -620,6 +651,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
   m.def("gemm_swiglu", &gemm_swiglu, "gate/up projection with the SwiGLU epilogue");
+  m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd,
+        "down-projection dgrad with the SwiGLU backward in the epilogue");
   m.def("gemm_tp", &gemm_tp, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("b_mn"),
         py::arg("pos"), py::arg("table"), py::arg("rope_cols"), py::arg("hd"), py::arg("mode"),
         py::arg("rank"), py::arg("P"), py::arg("seg"), py::arg("epoch"),

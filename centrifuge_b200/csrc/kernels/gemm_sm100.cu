@@ -47,6 +47,9 @@ struct GemmArgs {
   int dual_off;
   __nv_bfloat16* aux;
   long long ld_aux;
+  // kEpiSwiGLUBwd: aux = gu [*, 2F] (read; gate at column n, up at dual_off + n) of row
+  // aux_rows[m] (or m); D [M, 2F] receives d gate at column n and d up at dual_off + n
+  const int* aux_rows;
   // ---- tensor-parallel fusion.  Row segments: rank q owns rows [seg[q], seg[q+1]) of A / D
   // (device array [P + 1]; uniform shards in the forward, kept rows in the backward).  Flags
   // live in symmetric buffers peer_flags[q]: ready[P] at flag_ready, done[P] at flag_done.
@@ -197,6 +200,39 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, uint32_t taddr, 
           reinterpret_cast<uint4*>(gd)[j] = make_uint4(og[4 * j], og[4 * j + 1], og[4 * j + 2], og[4 * j + 3]);
           reinterpret_cast<uint4*>(ud)[j] = make_uint4(ou[4 * j], ou[4 * j + 1], ou[4 * j + 2], ou[4 * j + 3]);
           reinterpret_cast<uint4*>(hd)[j] = make_uint4(oh[4 * j], oh[4 * j + 1], oh[4 * j + 2], oh[4 * j + 3]);
+        }
+      }
+      continue;
+    }
+    if (EPI == kEpiSwiGLUBwd) {
+      uint32_t rd[32];
+      CFB_TMEM_LD32(taddr + c * 32, rd);
+      tmem_ld_wait();
+      if (row < p.M) {
+        const long long src = p.aux_rows ? p.aux_rows[row] : row;
+        const uint4* g4 = reinterpret_cast<const uint4*>(p.aux + src * p.ld_aux + col);
+        const uint4* u4 = reinterpret_cast<const uint4*>(p.aux + src * p.ld_aux + p.dual_off + col);
+        uint4* dg4 = reinterpret_cast<uint4*>(drow + col);
+        uint4* du4 = reinterpret_cast<uint4*>(drow + p.dual_off + col);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 gq = g4[j], uq = u4[j];
+          const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gq);
+          const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&uq);
+          uint32_t og[4], ou[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 g = __bfloat1622float2(gh[e]);
+            const float2 u = __bfloat1622float2(uh[e]);
+            const float d0 = __uint_as_float(rd[8 * j + 2 * e]) * p.alpha;
+            const float d1 = __uint_as_float(rd[8 * j + 2 * e + 1]) * p.alpha;
+            const float s0 = 1.f / (1.f + __expf(-g.x)), s1 = 1.f / (1.f + __expf(-g.y));
+            og[e] = pack_bf16x2(d0 * u.x * s0 * (1.f + g.x * (1.f - s0)),
+                                d1 * u.y * s1 * (1.f + g.y * (1.f - s1)));
+            ou[e] = pack_bf16x2(d0 * g.x * s0, d1 * g.y * s1);
+          }
+          dg4[j] = make_uint4(og[0], og[1], og[2], og[3]);
+          du4[j] = make_uint4(ou[0], ou[1], ou[2], ou[3]);
         }
       }
       continue;
@@ -990,6 +1026,9 @@ static int dispatch_epi(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
     case kEpiBF16Rope:  // forward projections only: both operands K-major
       if (a_mn || b_mn) return -4;
       return launch_gemm<BN, false, false, kEpiBF16Rope>(ta, tb, a, st, max_ctas);
+    case kEpiSwiGLUBwd:
+      if (a_mn || !b_mn) return -4;
+      return launch_gemm<BN, false, true, kEpiSwiGLUBwd>(ta, tb, a, st, max_ctas);
   }
   return -4;
 }
@@ -1049,6 +1088,9 @@ static int dispatch_pair(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
     case kEpiBF16Rope:
       if (a_mn || b_mn) return -4;
       return launch_gemm_pair<false, false, kEpiBF16Rope>(ta, tb, a, st);
+    case kEpiSwiGLUBwd:  // down-projection dgrad only: A K-major, B MN-major
+      if (a_mn || !b_mn) return -4;
+      return launch_gemm_pair<false, true, kEpiSwiGLUBwd>(ta, tb, a, st);
   }
   return -4;
 }
@@ -1105,11 +1147,19 @@ static GemmPlan plan_gemm(int M, int N, int K, int bn_req, bool can_split, bool 
   return best;
 }
 
+// operands of the dual-column epilogues (SwiGLU backward) that the other entries leave unset
+struct EpiExtra {
+  int dual_off;
+  const void* aux;
+  long long ld_aux;
+  const int* aux_rows;
+};
+
 static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, long long ldb,
                       int b_mn, void* D, long long ldd, int epi, const void* R, long long ldr,
                       int M, int N, int K, float alpha, int* err, int bn, int max_ctas,
                       const int* pos, const float* cs, int rope_cols, int hd,
-                      const CfbTpGemm* tp, cudaStream_t st) {
+                      const CfbTpGemm* tp, cudaStream_t st, const EpiExtra* ex = nullptr) {
   if (M <= 0 || N <= 0 || K <= 0) return -10;
   if ((N % 32) != 0 || (lda % 8) != 0 || (ldb % 8) != 0) return -11;
   if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
@@ -1163,9 +1213,10 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.cs = cs;
   a.rope_cols = rope_cols;
   a.hd = hd;
-  a.dual_off = 0;
-  a.aux = nullptr;
-  a.ld_aux = 0;
+  a.dual_off = ex ? ex->dual_off : 0;
+  a.aux = ex ? const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(ex->aux)) : nullptr;
+  a.ld_aux = ex ? ex->ld_aux : 0;
+  a.aux_rows = ex ? ex->aux_rows : nullptr;
   a.rank = 0;
   a.P = 1;
   a.seg = nullptr;
@@ -1238,7 +1289,7 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
 int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
                   int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st) {
-  if (epi == kEpiBF16Rope) return -4;
+  if (epi == kEpiBF16Rope || epi == kEpiSwiGLU || epi == kEpiSwiGLUBwd) return -4;
   return gemm_entry(A, lda, a_mn, B, ldb, b_mn, D, ldd, epi, R, ldr, M, N, K, alpha, err, bn,
                     max_ctas, nullptr, nullptr, 0, 0, nullptr, st);
 }
@@ -1286,6 +1337,16 @@ int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, 
   }();
   if (pair_on) return launch_gemm_pair<false, false, kEpiSwiGLU>(ta, tb, a, st);
   return launch_gemm<128, false, false, kEpiSwiGLU>(ta, tb, a, st, 0);
+}
+
+int cfb_gemm_swiglu_bwd(const void* dY, long long ld_dy, const void* Wd, long long ld_w,
+                        const void* gu, long long ld_gu, const int* gu_rows, void* dgu,
+                        long long ld_dgu, int M, int F, int K, int* err, cudaStream_t st) {
+  if ((ld_gu % 8) || (ld_dgu % 8) || (F % 8) || !gu) return -11;
+  if (reinterpret_cast<uintptr_t>(gu) & 15) return -12;
+  const EpiExtra ex{F, gu, ld_gu, gu_rows};
+  return gemm_entry(dY, ld_dy, 0, Wd, ld_w, 1, dgu, ld_dgu, kEpiSwiGLUBwd, nullptr, 0, M, F, K,
+                    1.0f, err, 0, 0, nullptr, nullptr, 0, 0, nullptr, st, &ex);
 }
 
 int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,

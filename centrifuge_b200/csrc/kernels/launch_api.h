@@ -6,7 +6,15 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-enum { kEpiBF16 = 0, kEpiBF16Resid = 1, kEpiF32 = 2, kEpiF32Acc = 3, kEpiBF16Rope = 4, kEpiSwiGLU = 5 };
+enum {
+  kEpiBF16 = 0,
+  kEpiBF16Resid = 1,
+  kEpiF32 = 2,
+  kEpiF32Acc = 3,
+  kEpiBF16Rope = 4,
+  kEpiSwiGLU = 5,
+  kEpiSwiGLUBwd = 6  // dgrad of the down projection -> d[gate; up] (see cfb_gemm_swiglu_bwd)
+};
 // `bn` value of cfb_gemm_bf16 that selects the 256 x 256 tile on a CTA pair (cta_group::2);
 // 128 / 256 select a single-CTA tile of that width, 0 lets the planner choose
 enum { kGemmTilePair = 512 };
@@ -21,6 +29,13 @@ int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long lo
 int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, void* GU,
                     long long ld_gu, void* Hout, long long ld_h, int M, int F, int K, int* err,
                     cudaStream_t st);
+// dgu[M, 2F] = SwiGLU backward of dh = dY[M, K] @ Wd[K, F] (Wd read MN-major: the down
+// projection's weight [H, F] with K = H), computed in the GEMM epilogue: with g, u the saved
+// gate / up of row gu_rows[m] (or m) of gu [*, 2F] (ld_gu), dgu[m, f] = dh * u * s * (1 + g (1 - s))
+// and dgu[m, F + f] = dh * g * s, s = sigmoid(g).  dh itself is never stored.
+int cfb_gemm_swiglu_bwd(const void* dY, long long ld_dy, const void* Wd, long long ld_w,
+                        const void* gu, long long ld_gu, const int* gu_rows, void* dgu,
+                        long long ld_dgu, int M, int F, int K, int* err, cudaStream_t st);
 
 // Tensor-parallel fusion of a GEMM (A [M, K] K-major; B [N, K] K-major or, with b_mn, [K, N])
 // with a collective over NVLink (gemm_sm100.cu), in one cooperative launch.  The M rows are

@@ -97,6 +97,24 @@ def linear_fwd_swiglu(x: torch.Tensor, w: torch.Tensor):
     return gu, h
 
 
+def linear_dgrad_swiglu(dy: torch.Tensor, wd: torch.Tensor, gu: torch.Tensor,
+                        gu_rows: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``d[gate; up]`` of ``h = silu(gate) * up`` given ``dy`` at the down projection's output:
+    ``dh = dy wd`` (``wd [H, F]``) feeds the SwiGLU backward in the GEMM epilogue, with the saved
+    ``gu`` rows ``gu_rows`` (kept rows of the forward's ``gu``; all rows when ``None``).
+    Returns ``dgu [T, 2F]``; ``dh`` is never materialised."""
+    F = wd.shape[1]
+    dgu = torch.empty(dy.shape[0], 2 * F, dtype=dy.dtype, device=dy.device)
+    if not dy.is_cuda:
+        from . import fused
+        dh = (dy.float() @ wd.float()).to(dy.dtype)
+        return fused.swiglu_bwd(dh, gu, gu_rows, out=dgu)
+    if F % 32:
+        raise ValueError(f"linear_dgrad_swiglu: F = {F} is not a multiple of 32")
+    kernels().gemm_swiglu_bwd(dy, wd, gu, gu_rows, dgu)
+    return dgu
+
+
 def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = None,
                  resid: Optional[torch.Tensor] = None) -> torch.Tensor:
     if out is None:
