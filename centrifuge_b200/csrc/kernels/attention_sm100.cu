@@ -9,12 +9,12 @@
 //               done, a V slot only after P_j V_j, so K loads run well ahead of the softmax
 //   warp 1      MMA issuer:   S_j into one of two TMEM tiles (128 x 128 fp32), then
 //                             O += P_j V_j into the TMEM accumulators
-//   warps 2-9   softmax:      two threads per query row (= TMEM lane): warps w and w+4 share a
-//                             lane quadrant and take keys [0, 64) / [64, 128) of every step.
-//                             Each half keeps its own running max, row sum and O accumulator
-//                             (O0, O1 in TMEM, fed by two K=64 PV MMAs), so the halves never
-//                             synchronise per step; the epilogue merges them once
-//                             (O = O0 2^(m0-m) + O1 2^(m1-m), same for l).  Online softmax in
+//   warps 2..   softmax:      NQ = 2 threads per query row (= TMEM lane): warps w, w+4 share a
+//                             lane quadrant and take key groups [0, 64), [64, 128) of every step.
+//                             Each group keeps its own running max, row sum and O accumulator
+//                             (O_0 .. O_{NQ-1} in TMEM, fed by one PV MMA chain per group), so
+//                             the groups never synchronise per step; the epilogue merges them
+//                             once (O = sum_q O_q 2^(m_q-m), same for l).  Online softmax in
 //                             fp32 with one FMA + ex2 per score; P (bf16) is written back into
 //                             TMEM over the thread's own S columns and feeds P V as the TMEM A
 //                             operand, so P never touches shared memory; a running max only
@@ -50,9 +50,14 @@ struct Smem {
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + QBUF * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KV_STAGES * KV_TILE;
-  static constexpr int OFF_RED = OFF_V + KV_STAGES * KV_TILE;  // epilogue exchange: [4][128] fp32
-  static constexpr int OFF_FLAG = OFF_RED + 4 * BM * 4;  // [2 half][128] exchange counters
-  static constexpr int OFF_BAR = OFF_FLAG + 2 * BM * 4;
+  // key groups (threads) per query row.  Four groups (16 softmax warps) at hd 64 measured
+  // slower than two (307 vs 441 TFLOP/s at B8 S2048 32q/4kv): the per-group PV MMAs become
+  // K = 32 chains and the epilogue merge costs more than the extra warps hide.
+  static constexpr int NQ = 2;
+  static constexpr int THREADS = 64 + 128 * NQ;           // TMA + MMA warps, 4 NQ softmax warps
+  static constexpr int OFF_RED = OFF_V + KV_STAGES * KV_TILE;  // exchange: [2][NQ][128] fp32
+  static constexpr int OFF_FLAG = OFF_RED + 2 * NQ * BM * 4;   // [NQ][128] exchange counters
+  static constexpr int OFF_BAR = OFF_FLAG + NQ * BM * 4;
   static constexpr int BYTES = OFF_BAR + 256 + 1024;     // + barriers + alignment slack
   static_assert(KV_STAGES <= MAX_RING && QBUF <= 2, "rings");
   static_assert(BYTES <= 232448, "shared memory per CTA");
@@ -113,40 +118,50 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                : "memory");
 }
 
-// Exchange one float per row with the partner warp of the same lane quadrant.  Each side
-// publishes its value and a sequence number in shared memory and spins (bounded) until the
-// partner's sequence number arrives.  Values use slot pair `slot_base` (+ half); a slot is only
-// rewritten two exchanges later, after the partner has provably read it.  Returns false if the
-// wait gave up.
-__device__ __forceinline__ bool pair_exchange(float* vals, volatile int* flags, int slot_base,
-                                              int half, int r, int seq, float mine, float& theirs,
-                                              volatile int* abort_flag, int* err) {
+// Exchange one float per row among the NQ groups of the same lane quadrant.  Each thread
+// publishes its value in slot `slot` and a sequence number in shared memory, then spins
+// (bounded) until every other group's sequence number arrives, and returns all NQ values
+// (vals_out[q], its own included).  A slot is only rewritten two exchanges later, after every
+// other group has provably read it (it published the following exchange's sequence number only
+// after reading).  Returns false if the wait gave up.
+template <int NQ>
+__device__ __forceinline__ bool group_exchange(float* vals, volatile int* flags, int slot,
+                                               int grp, int r, int seq, float mine,
+                                               float (&vals_out)[NQ], volatile int* abort_flag,
+                                               int* err) {
   constexpr int BMr = 128;
-  vals[(slot_base + half) * BMr + r] = mine;
+  vals[(slot * NQ + grp) * BMr + r] = mine;
   __threadfence_block();
-  flags[half * BMr + r] = seq;
+  flags[grp * BMr + r] = seq;
   const uint64_t t0 = globaltimer_ns();
-  uint32_t spins = 0;
-  while (flags[(half ^ 1) * BMr + r] < seq) {
-    if ((++spins & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        atomicCAS(err, 0, kErrWaitSoftmax);
-        return false;
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    if (q == grp) continue;
+    uint32_t spins = 0;
+    while (flags[q * BMr + r] < seq) {
+      if ((++spins & 255u) == 0) {
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          *abort_flag = 1;
+          atomicCAS(err, 0, kErrWaitSoftmax);
+          return false;
+        }
       }
     }
   }
   __threadfence_block();
-  theirs = vals[(slot_base + (half ^ 1)) * BMr + r];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) vals_out[q] = q == grp ? mine : vals[(slot * NQ + q) * BMr + r];
   return true;
 }
 
 template <int HD>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(Smem<HD>::THREADS, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   using L = Smem<HD>;
-  constexpr int QBUF = L::QBUF, KVS = L::KV_STAGES;
+  constexpr int QBUF = L::QBUF, KVS = L::KV_STAGES, NQ = L::NQ;
+  constexpr int NSW = 4 * NQ;  // softmax warps
+  constexpr int CW = BN / NQ;  // keys per softmax thread per step
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -169,16 +184,16 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&bar->s_full[s]), 1);
-      mbar_init(smem_u32(&bar->s_free[s]), 8);
+      mbar_init(smem_u32(&bar->s_free[s]), NSW);
     }
-    mbar_init(smem_u32(&bar->p_ready), 8);
+    mbar_init(smem_u32(&bar->p_ready), NSW);
     mbar_init(smem_u32(&bar->o_done), 1);
-    mbar_init(smem_u32(&bar->o_free), 8);
+    mbar_init(smem_u32(&bar->o_free), NSW);
     mbar_init(smem_u32(&bar->drain), 1);
     bar->abort = 0;
     fence_mbar_init();
   }
-  for (int i = threadIdx.x; i < 2 * BM; i += blockDim.x)
+  for (int i = threadIdx.x; i < NQ * BM; i += blockDim.x)
     reinterpret_cast<volatile int*>(smem + L::OFF_FLAG)[i] = 0;
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
   if (warp == 1) {
@@ -190,7 +205,8 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = bar->tmem_slot;
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t o_col = 2 * BN;  // O0, O1 accumulators (HD columns each) after the S tiles
+  const uint32_t o_col = 2 * BN;  // O_0 .. O_{NQ-1} (HD columns each) after the S tiles
+  static_assert(2 * BN + NQ * HD <= 512, "TMEM columns");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -316,11 +332,12 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t acc0 = j > 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            // keys [0, 64) accumulate into O0, keys [64, 128) into O1; P_j (bf16) sits in the
-            // first 32 columns of each half of S_j's TMEM tile
-            const int hh = kk >> 2;
-            umma_bf16_ts(tmem + o_col + hh * HD, pa + hh * 64 + (kk & 3) * 8,
-                         vd + ((kk * 2048) >> 4), IDESC_O, (kk & 3) > 0 ? 1u : acc0);
+            // keys of group q = [q CW, (q + 1) CW) accumulate into O_q; P_j (bf16, two per
+            // column) sits in the first CW / 2 columns of the group's CW columns of S_j
+            constexpr int KPG = CW / 16;  // K steps per group
+            const int q = kk / KPG, kq = kk % KPG;
+            umma_bf16_ts(tmem + o_col + q * HD, pa + q * CW + kq * 8, vd + ((kk * 2048) >> 4),
+                         IDESC_O, kq > 0 ? 1u : acc0);
           }
           umma_commit(smem_u32(&bar->o_done));
           umma_commit(smem_u32(&bar->v_empty[st]));
@@ -341,13 +358,12 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue, warps 2-9
-    constexpr int HALF = BN / 2;       // keys per thread per step
-    constexpr int OH = HD / 2;         // output columns per thread in the epilogue
+    constexpr int OH = HD / NQ;        // output columns per thread in the epilogue
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;  // 0: warps 2-5, 1: warps 6-9
+    const int grp = (warp - 2) >> 2;   // key group: warps 2-5 -> 0, 6-9 -> 1, ...
     const int r = quad * 32 + lane;    // query row in the tile == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const uint32_t my_o = o_col + half * HD;
+    const uint32_t my_o = o_col + grp * HD;
     const float c = p.scale_log2;
     float* red = reinterpret_cast<float*>(smem + L::OFF_RED);
     volatile int* xflag = reinterpret_cast<volatile int*>(smem + L::OFF_FLAG);
@@ -362,8 +378,8 @@ __global__ void __launch_bounds__(320, 1)
       const Item t = decode(id, p);
       const int q0 = t.qb * BM;
       const int qpos = q0 + r;
-      float m_ref = -CUDART_INF_F;  // running reference max of this half, log2 units
-      float l = 0.f;                // running row sum of this half
+      float m_ref = -CUDART_INF_F;  // running reference max of this group, log2 units
+      float l = 0.f;                // running row sum of this group
       for (int j = 0; j < t.nkb; ++j) {
         const int gg = g + j, sb = gg & 1;
         if (!mbar_wait(smem_u32(&bar->s_full[sb]), (gg >> 1) & 1, abort_flag, p.err,
@@ -372,27 +388,27 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        float sv[HALF];
+        float sv[CW];
         {
           uint32_t* su = reinterpret_cast<uint32_t*>(sv);
 #pragma unroll
-          for (int cc = 0; cc < HALF / 32; ++cc)
-            CFB_TMEM_LD32(lane_addr + sb * BN + half * HALF + cc * 32, (su + cc * 32));
+          for (int cc = 0; cc < CW / 32; ++cc)
+            CFB_TMEM_LD32(lane_addr + sb * BN + grp * CW + cc * 32, (su + cc * 32));
         }
         tmem_ld_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&bar->s_free[sb]));
-        const int k0 = j * BN + half * HALF;
-        if ((k0 + HALF - 1 > q0) || (k0 + HALF > p.S)) {  // diagonal / ragged block: mask
-          const int lim = min(qpos, p.S - 1) - k0;      // keys with index <= lim are visible
+        const int k0 = j * BN + grp * CW;
+        if ((k0 + CW - 1 > q0) || (k0 + CW > p.S)) {  // diagonal / ragged block: mask
+          const int lim = min(qpos, p.S - 1) - k0;  // keys with index <= lim are visible
 #pragma unroll
-          for (int i = 0; i < HALF; ++i)
+          for (int i = 0; i < CW; ++i)
             if (i > lim) sv[i] = -CUDART_INF_F;
         }
         float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-        for (int i = 0; i < HALF; i += 8) {  // four independent max chains
+        for (int i = 0; i < CW; i += 8) {  // four independent max chains
 #pragma unroll
           for (int q = 0; q < 4; ++q) m4[q] = fmax3f(m4[q], sv[i + 2 * q], sv[i + 2 * q + 1]);
         }
@@ -407,9 +423,9 @@ __global__ void __launch_bounds__(320, 1)
         }
         const float nref = (m_ref == -CUDART_INF_F) ? 0.f : -m_ref;
         float rs[4] = {0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[HALF / 2];
+        uint32_t pk[CW / 2];
 #pragma unroll
-        for (int i = 0; i < HALF / 2; ++i) {
+        for (int i = 0; i < CW / 2; ++i) {
           const float e0 = ex2_approx(fmaf(sv[2 * i], c, nref));
           const float e1 = ex2_approx(fmaf(sv[2 * i + 1], c, nref));
           rs[(2 * i) & 3] += e0;
@@ -426,9 +442,13 @@ __global__ void __launch_bounds__(320, 1)
           break;
         }
         tc_fence_after();
-        // P_j (bf16, 32 columns) overwrites the first half of this thread's own 64 S columns
-        CFB_TMEM_ST32(lane_addr + sb * BN + half * HALF, pk);
-        if (j > 0 && __any_sync(0xffffffffu, grow)) {  // a grown max rescales this half's O
+        // P_j (bf16, CW / 2 columns) overwrites the first half of this thread's CW S columns
+        if constexpr (CW == 64) {
+          CFB_TMEM_ST32(lane_addr + sb * BN + grp * CW, pk);
+        } else {
+          CFB_TMEM_ST16(lane_addr + sb * BN + grp * CW, pk);
+        }
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {  // a grown max rescales this group's O
 #pragma unroll
           for (int cc = 0; cc < HD / 32; ++cc) {
             uint32_t o[32];
@@ -445,49 +465,62 @@ __global__ void __launch_bounds__(320, 1)
         if (lane == 0) mbar_arrive(smem_u32(&bar->p_ready));
       }
       if (!ok) break;
-      // epilogue: merge the two halves' (m, l, O) once, write O / l and the LSE
+      // epilogue: merge the NQ groups' (m, l, O) once, write O / l and the LSE
       const int gl = g + t.nkb - 1;
       if (!mbar_wait(smem_u32(&bar->o_done), gl & 1, abort_flag, p.err, kErrWaitSoftmax)) break;
       tc_fence_after();
-      float m_o = 0.f, l_o = 0.f;
-      if (!pair_exchange(red, xflag, 0, half, r, 2 * k + 1, m_ref, m_o, abort_flag, p.err) ||
-          !pair_exchange(red, xflag, 2, half, r, 2 * k + 2, l, l_o, abort_flag, p.err))
+      float mq[NQ], lq[NQ];
+      if (!group_exchange<NQ>(red, xflag, 0, grp, r, 2 * k + 1, m_ref, mq, abort_flag, p.err) ||
+          !group_exchange<NQ>(red, xflag, 1, grp, r, 2 * k + 2, l, lq, abort_flag, p.err))
         break;
-      const float m0 = half == 0 ? m_ref : m_o, m1 = half == 0 ? m_o : m_ref;
-      const float l0 = half == 0 ? l : l_o, l1 = half == 0 ? l_o : l;
-      const float M = fmaxf(m0, m1);
-      const float f0 = (m0 == -CUDART_INF_F) ? 0.f : ex2_approx(m0 - M);
-      const float f1 = (m1 == -CUDART_INF_F) ? 0.f : ex2_approx(m1 - M);
-      const float Lt = l0 * f0 + l1 * f1;
+      float M = mq[0];
+#pragma unroll
+      for (int q = 1; q < NQ; ++q) M = fmaxf(M, mq[q]);
+      float fq[NQ], Lt = 0.f;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        fq[q] = (mq[q] == -CUDART_INF_F) ? 0.f : ex2_approx(mq[q] - M);
+        Lt += lq[q] * fq[q];
+      }
       const float inv = Lt > 0.f ? 1.f / Lt : 0.f;
-      const float g0 = f0 * inv, g1 = f1 * inv;
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) fq[q] *= inv;
       const int row0 = t.b * p.S;
+      // this thread writes output columns [grp OH, (grp + 1) OH) of its row
       __nv_bfloat16* dst = p.out + static_cast<long long>(row0 + min(qpos, p.S - 1)) * p.ld_out +
-                           t.h * HD + half * OH;
+                           t.h * HD + grp * OH;
+      constexpr int CH = OH < 32 ? OH : 32;  // columns per TMEM load
 #pragma unroll
-      for (int cc = 0; cc < OH / 32; ++cc) {
-        uint32_t a0[32], a1[32];
-        CFB_TMEM_LD32(lane_addr + o_col + half * OH + cc * 32, a0);
-        CFB_TMEM_LD32(lane_addr + o_col + HD + half * OH + cc * 32, a1);
-        tmem_ld_wait();
+      for (int cc = 0; cc < OH / CH; ++cc) {
+        float v[CH];
+#pragma unroll
+        for (int e = 0; e < CH; ++e) v[e] = 0.f;
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          uint32_t a[CH];
+          if constexpr (CH == 32) {
+            CFB_TMEM_LD32(lane_addr + o_col + q * HD + grp * OH + cc * CH, a);
+          } else {
+            CFB_TMEM_LD16(lane_addr + o_col + q * HD + grp * OH + cc * CH, a);
+          }
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < CH; ++e) v[e] = fmaf(__uint_as_float(a[e]), fq[q], v[e]);
+        }
         if (qpos < p.S) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cc * CH);
 #pragma unroll
-          for (int kq = 0; kq < 4; ++kq) {
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e)
-              v[e] = __uint_as_float(a0[8 * kq + e]) * g0 + __uint_as_float(a1[8 * kq + e]) * g1;
+          for (int kq = 0; kq < CH / 8; ++kq) {
             uint4 u;
-            u.x = pack_bf16x2(v[0], v[1]);
-            u.y = pack_bf16x2(v[2], v[3]);
-            u.z = pack_bf16x2(v[4], v[5]);
-            u.w = pack_bf16x2(v[6], v[7]);
+            u.x = pack_bf16x2(v[8 * kq + 0], v[8 * kq + 1]);
+            u.y = pack_bf16x2(v[8 * kq + 2], v[8 * kq + 3]);
+            u.z = pack_bf16x2(v[8 * kq + 4], v[8 * kq + 5]);
+            u.w = pack_bf16x2(v[8 * kq + 6], v[8 * kq + 7]);
             d4[kq] = u;
           }
         }
       }
-      if (qpos < p.S && half == 0)
+      if (qpos < p.S && grp == 0)
         p.lse[static_cast<long long>(row0 + qpos) * p.nh + t.h] = (M + log2f(Lt)) * kLn2;
       // O read: the next item's first PV may overwrite it
       tc_fence_before();
@@ -547,7 +580,7 @@ int launch(const void* qkv, long long ld, void* out, long long ld_out, float* ls
     configured = true;
   }
   const int grid = p.n_items < n_sm ? p.n_items : n_sm;
-  kern<<<grid, 320, Smem<HD>::BYTES, st>>>(tm, p);
+  kern<<<grid, Smem<HD>::THREADS, Smem<HD>::BYTES, st>>>(tm, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

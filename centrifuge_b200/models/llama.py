@@ -242,9 +242,12 @@ class LlamaCore(torch.nn.Module):
             # ---- MLP
             h_k = self._gather(L["h"], rows)
             G.linear_wgrad(dx, h_k, g[pre + "wd"])
+            dh = G.linear_dgrad(dx, p[pre + "wd"])
             del h_k
-            # down-projection dgrad with the SwiGLU backward in its epilogue
-            dgu = G.linear_dgrad_swiglu(dx, p[pre + "wd"], L["gu"], rows)
+            # a separate pass: the SwiGLU backward in the dgrad epilogue (linear_dgrad_swiglu)
+            # measured slower at these shapes (its gathered gate/up reads stall the epilogue)
+            dgu = fused.swiglu_bwd(dh, L["gu"], rows)
+            del dh
             xn2_k = self._gather(L["xn2"], rows)
             G.linear_wgrad(dgu, xn2_k, g[pre + "wgu"])
             dxn2 = G.linear_dgrad(dgu, p[pre + "wgu"])

@@ -290,9 +290,10 @@ class TPLlamaCore(torch.nn.Module):
             dY = ag(dx)
             h_k = gat(L["h"])
             G.linear_wgrad(dY, h_k, g[pre + "wd"])
-            del h_k
-            dgu = G.linear_dgrad_swiglu(dY, p[pre + "wd"], L["gu"], rows)
-            del dY
+            dh = G.linear_dgrad(dY, p[pre + "wd"])
+            del h_k, dY
+            dgu = fused.swiglu_bwd(dh, L["gu"], rows)
+            del dh
             xn2_k = gat(L["xn2"])
             G.linear_wgrad(dgu, xn2_k, g[pre + "wgu"])
             dxn2_p = rs(G.linear_dgrad(dgu, p[pre + "wgu"]))
