@@ -64,7 +64,8 @@ def main():
     layers = stage_layers(cfg.num_hidden_layers, a.pp, g.stage)
     core = TPLlamaCore(cfg, g.tp_group, device=dev, first=layers.start, last=layers.stop,
                        has_embed=g.stage == 0, has_head=g.stage == a.pp - 1)
-    core.use_fused_comm = a.comm == "fused" and a.pp == 1 and a.tp > 1
+    core.use_fused_comm = a.comm == "fused" and a.tp > 1
+    core.comm_sets = a.pp  # 1F1B keeps up to pp forwarded micro-batches per stage
     gen = torch.Generator(device=dev).manual_seed(1234 + g.stage * 100 + g.tp_rank)
     for name, p in core.flat.params.items():
         if p.dim() == 1:

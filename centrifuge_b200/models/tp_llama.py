@@ -111,6 +111,11 @@ class TPLlamaCore(torch.nn.Module):
         # The gather buffers double as saved activations until the next forward, so this is for
         # schedules with one micro-batch in flight (no pipeline interleaving).
         self.use_fused_comm = False
+        # micro-batches whose fused-forward activations may be alive at once (1F1B pipeline
+        # stages keep up to `pp` forwarded micro-batches before their backward): each gets its
+        # own set of gather slots
+        self.comm_sets = 1
+        self._fwd_count = 0
         self._comm = None
 
     def reduce_replicated_grads(self) -> None:
@@ -204,12 +209,15 @@ class TPLlamaCore(torch.nn.Module):
         sv["head"] = dict(x=x, xf=xf, rstdf=rf, logits=logits, labels=lab, lse=lse_ce)
         return loss.view(B, S)[:, :-1].contiguous(), sv
 
+    def _slots_per_set(self) -> int:
+        # xn, xn2 per layer, the final norm, two for the backward's gathers
+        return 2 * len(self.layer_ids) + 3
+
     def _fused_comm(self, T: int):
         if self._comm is None or self._comm.T != T:
             from ..parallel.tp_fused import TPFusedComm
-            # slots: xn, xn2 per layer, the final norm, two for the backward's gathers
             self._comm = TPFusedComm(self.tp, T, self.cfg.hidden_size,
-                                     2 * len(self.layer_ids) + 3, self.device)
+                                     self.comm_sets * self._slots_per_set(), self.device)
         return self._comm
 
     def _forward_fused(self, comm, x, input_ids, labels, B, S, sv, pos):
@@ -218,16 +226,20 @@ class TPLlamaCore(torch.nn.Module):
         p, cfg, tp = self.flat.params, self.cfg, self.tp
         nh, nkv, hd = self.nh, self.nkv, self.hd
         eps = cfg.rms_norm_eps
+        # this micro-batch's slot set (its gathered rows stay valid until its backward)
+        base = (self._fwd_count % self.comm_sets) * self._slots_per_set()
+        self._fwd_count += 1
+        sv["comm_base"] = base
         for li, i in enumerate(self.layer_ids):
             pre = f"layers.{i}."
             L = {"x": x}
-            xn, r1 = comm.rmsnorm_local(x, p[pre + "ln1"], eps, 2 * li)
-            qkv = comm.gemm_ag(xn, p[pre + "wqkv"], 2 * li,
+            xn, r1 = comm.rmsnorm_local(x, p[pre + "ln1"], eps, base + 2 * li)
+            qkv = comm.gemm_ag(xn, p[pre + "wqkv"], base + 2 * li,
                                rope=(pos, self._rope, (nh + nkv) * hd, hd))
             o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd, scale=self.scale)
             x2 = comm.gemm_rs(o, p[pre + "wo"], x)
-            xn2, r2 = comm.rmsnorm_local(x2, p[pre + "ln2"], eps, 2 * li + 1)
-            gu = comm.gemm_ag(xn2, p[pre + "wgu"], 2 * li + 1)
+            xn2, r2 = comm.rmsnorm_local(x2, p[pre + "ln2"], eps, base + 2 * li + 1)
+            gu = comm.gemm_ag(xn2, p[pre + "wgu"], base + 2 * li + 1)
             h = fused.swiglu_fwd(gu)
             x = comm.gemm_rs(h, p[pre + "wd"], x2)
             L.update(xn=xn, rstd1=r1, qkv=qkv, o=o, lse=lse, x2=x2, xn2=xn2, rstd2=r2, gu=gu, h=h)
@@ -235,7 +247,7 @@ class TPLlamaCore(torch.nn.Module):
         sv["fused"] = True
         if not self.has_head:
             return x, sv
-        fslot = 2 * len(self.layer_ids)
+        fslot = base + 2 * len(self.layer_ids)
         xf, rf = comm.rmsnorm_local(x, p["norm"], eps, fslot)
         logits = comm.gemm_ag(xf, p["lm_head"], fslot)
         return self._head_loss(logits, x, xf, rf, input_ids, labels, B, S, sv)
@@ -345,28 +357,32 @@ def _backward_fused_impl(self, sv, grad_out, state, lay, rows, Sk, pos_flat, pos
     seg = Segments(lay.counts, self.device)
     C = lay.C
     local = None if lay.identity else lay.local
-    slot_a = 2 * len(self.layer_ids) + 1
+    slot_a = sv.get("comm_base", 0) + 2 * len(self.layer_ids) + 1
     slot_b = slot_a + 1
 
     def gat(t):
         return t if rows is None else _gather(t, rows)
 
-    assert self.has_head, "the fused backward runs on a full TP model (no pipeline stages)"
-    hd_ = sv["head"]
-    dl = grad_out.float()
-    if state is not None and dl.shape[1] == S - 1:
-        dl = torch.gather(dl, 1, pos2d[:, :-1].long())
-    dl = torch.cat([dl, torch.zeros(B, 1, device=dl.device, dtype=dl.dtype)], 1)
-    dloss = dl.reshape(-1).contiguous()
-    dlogits = fused.ce_bwd(hd_["logits"], hd_["labels"], hd_["lse"], dloss, rows,
-                           vocab_start=self.vocab_start)
-    xf_k = gat(hd_["xf"])
-    G.linear_wgrad(dlogits, xf_k, g["lm_head"])
-    dxf_p = comm.gemm_rs(dlogits, p["lm_head"], None, seg=seg, b_mn=True, out_rows=C)
-    del dlogits, xf_k
+    if self.has_head:
+        hd_ = sv["head"]
+        dl = grad_out.float()
+        if state is not None and dl.shape[1] == S - 1:
+            dl = torch.gather(dl, 1, pos2d[:, :-1].long())
+        dl = torch.cat([dl, torch.zeros(B, 1, device=dl.device, dtype=dl.dtype)], 1)
+        dloss = dl.reshape(-1).contiguous()
+        dlogits = fused.ce_bwd(hd_["logits"], hd_["labels"], hd_["lse"], dloss, rows,
+                               vocab_start=self.vocab_start)
+        xf_k = gat(hd_["xf"])
+        G.linear_wgrad(dlogits, xf_k, g["lm_head"])
+        dxf_p = comm.gemm_rs(dlogits, p["lm_head"], None, seg=seg, b_mn=True, out_rows=C)
+        del dlogits, xf_k
+        # dx of the final norm; its kept rows are all-gathered by the last layer's down dgrad
+        dx = fused.rmsnorm_bwd(dxf_p, hd_["x"], hd_["rstdf"], p["norm"], g["norm"], x_rows=local)
+    else:
+        # a pipeline stage below the head: the gradient of its output, this rank's kept rows
+        # (padded local layout, as this function returns it)
+        dx = grad_out.contiguous()
     layers = list(enumerate(self.layer_ids))
-    # dx of the final norm; its kept rows are all-gathered by the last layer's down dgrad
-    dx = fused.rmsnorm_bwd(dxf_p, hd_["x"], hd_["rstdf"], p["norm"], g["norm"], x_rows=local)
     dYg = comm.place_rows(dx, slot_a, seg)
     for li, i in reversed(layers):
         L = sv["layers"][li]

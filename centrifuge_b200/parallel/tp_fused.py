@@ -22,7 +22,9 @@ Rows are split into per-rank segments (:class:`Segments`): uniform sequence-para
 the forward, each rank's kept rows (compact global order) in the filtered backward, so the
 GEMMs see exactly the kept rows.  Buffers live in ``torch.distributed._symmetric_memory``.  The
 gather buffers are per call site ("slots", two per layer) and double as the saved activations
-of the backward, so a slot is rewritten only by the next micro-batch's forward; the receive
+of the backward, so a slot is rewritten only by a later micro-batch's forward: the model keeps
+one set of slots per micro-batch that can be in flight (one without pipelining, ``pp`` in a 1F1B
+pipeline stage, whose TP group is then the stage's subgroup); the receive
 partial buffers alternate by epoch and a GEMM of epoch e waits until every rank finished
 reading epoch e - 2.  Flags carry monotonically increasing epochs (never reset); every rank issues the same
 sequence of fused calls, so epochs agree across the group.  All waits are bounded (20 s) and

@@ -154,3 +154,87 @@ def test_tp2_fused_collectives_match_nccl():
         for dl, dg in rows:
             assert dl < 1e-2, (rank, kind, rows)
             assert dg < 3e-2, (rank, kind, rows)
+
+
+def _pp_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from centrifuge_b200.config import tiny_llama_test
+        from centrifuge_b200.models.tp_llama import TPLlamaCore
+        from centrifuge_b200.ops import kernels
+        from centrifuge_b200.parallel.pipeline import PipelineTrainer, build_groups, stage_layers
+        from centrifuge_b200.parallel.zero import ZeroAdamW
+        cfg = tiny_llama_test(layers=4, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=1024,
+                              head_dim=64)
+        cfg.max_position_embeddings = 512
+        os.environ["CFB_NODE_TRACING_FILE"] = f"/tmp/cfb_pp_dims_{rank}.txt"
+        g = build_groups(2, 2)
+        layers = stage_layers(cfg.num_hidden_layers, 2, g.stage)
+        core = TPLlamaCore(cfg, g.tp_group, device="cuda", first=layers.start, last=layers.stop,
+                           has_embed=g.stage == 0, has_head=g.stage == 1)
+        core.comm_sets = 2
+        torch.manual_seed(7 + 10 * g.stage + g.tp_rank)
+        for v in core.flat.params.values():
+            v.copy_(0.05 * torch.randn_like(v, dtype=torch.float32))
+        init = core.flat.data.clone()
+        gen = torch.Generator().manual_seed(5)
+        M, B, S = 4, 1, 512
+        batches = [(torch.randint(0, cfg.vocab_size, (B, S), generator=gen).cuda(),
+                    torch.exp(1.0 + 0.5 * torch.randn(B, S - 1, generator=gen)).cuda())
+                   for _ in range(M)]
+        res = []
+        for fused in (False, True, True):  # the second fused step reuses the slot sets
+            core.flat.data.copy_(init)
+            core.use_fused_comm = fused
+            opt = ZeroAdamW(core.flat, group=None, lr=1e-4, grad_clip=1.0,
+                            norm_group=dist.group.WORLD,
+                            replicated_ranges=core.replicated_ranges(), replication=2)
+            grads = {}
+            opt.pre_step_hooks.append(lambda: grads.update(
+                {"all": core.flat.grad.detach().float().clone()}))
+            tr = PipelineTrainer(core, opt, g, drop_rate=0.5, num_microbatches=M)
+            loss = tr.train_step(batches)
+            torch.cuda.synchronize()
+            res.append((None if loss is None else float(loss), grads["all"]))
+        l0, g0 = res[0]
+        out = []
+        for l1, g1 in res[1:]:
+            dl = 0.0 if l0 is None else abs(l1 - l0) / abs(l0)
+            out.append((dl, float((g1 - g0).norm() / (g0.norm() + 1e-12))))
+        q.put((rank, out, kernels().gemm_error_word(rank, True),
+               core._comm.kind if core._comm is not None else "none"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_pp2_fused_collectives_match_nccl():
+    """Tensor parallel 2 x 1F1B pipeline 2 with the sequence-parallel collectives fused into
+    the GEMMs inside every stage (each in-flight micro-batch on its own gather slots) gives the
+    NCCL pipeline's loss and gradients, over two steps."""
+    import torch.multiprocessing as mp
+
+    from tests.dist_utils import free_port
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_pp_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=300) for _ in range(4)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, rows, err_word, kind in outs:
+        assert err_word == 0, (rank, err_word)
+        for dl, dg in rows:
+            assert dl < 1e-2, (rank, kind, rows)
+            assert dg < 3e-2, (rank, kind, rows)
