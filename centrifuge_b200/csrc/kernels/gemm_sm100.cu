@@ -31,6 +31,10 @@ struct GemmArgs {
   // split-K (kEpiF32Acc only): every output tile is computed as ksplit work units over
   // consecutive k-block ranges, each adding its partial sum into D with fp32 vector reductions
   int ksplit;
+  // kEpiF32Acc: add into D with fp32 vector reductions (no read of D on the SM, so the
+  // epilogue never waits on memory; with one unit per tile each element gets exactly one add,
+  // the same result as load + add + store) instead of load + add + store
+  int acc_red;
   void* D;
   long long ldd;
   const __nv_bfloat16* R;
@@ -166,6 +170,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, uint32_t taddr, 
                                              int n0) {
   constexpr bool DUAL = EPI == kEpiSwiGLU;
   const int ksplit = p.ksplit;
+  (void)ksplit;
   __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
@@ -310,8 +315,9 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, uint32_t taddr, 
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          if (EPI == kEpiF32Acc && ksplit > 1) {
-            // the k-splits of this tile add into D concurrently (fp32, order not fixed)
+          if (EPI == kEpiF32Acc && (ksplit > 1 || p.acc_red)) {
+            // with split-K the k-splits of this tile add into D concurrently (fp32, order
+            // not fixed)
             asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
                              d4 + j),
                          "f"(o.x), "f"(o.y), "f"(o.z), "f"(o.w)
@@ -1175,6 +1181,11 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
     const char* e = std::getenv("CFB_GEMM_PAIR");
     return !(e && e[0] == '0');
   }();
+  // CFB_GEMM_ACC_RED=0: fp32-accumulate epilogues load, add and store instead of reducing
+  static const bool acc_red = [] {
+    const char* e = std::getenv("CFB_GEMM_ACC_RED");
+    return !(e && e[0] == '0');
+  }();
   int ksplit = 1;
   bool pair = false;
   if (!tp && max_ctas <= 0 && epi != kEpiSwiGLU) {
@@ -1203,6 +1214,7 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.N = N;
   a.K = K;
   a.ksplit = ksplit;
+  a.acc_red = (acc_red && (ldd % 4) == 0) ? 1 : 0;
   a.D = D;
   a.ldd = ldd;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
