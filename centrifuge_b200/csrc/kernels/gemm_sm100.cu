@@ -162,6 +162,13 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   tn = r / gsize;
 }
 
+__device__ __forceinline__ float silu_tanh(float g) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+  const float hg = 0.5f * g;
+  return fmaf(hg, t, hg);
+}
+
 // Epilogue of one accumulator row (TMEM lane) of a 128 x BN tile: tcgen05.ld of the fp32
 // accumulator at `taddr` (this warp's lane quadrant), then the EPI-specific conversion and
 // global stores of row `row`, columns [n0, n0 + BN) (clipped to N).
@@ -194,8 +201,9 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, uint32_t taddr, 
           // silu of the bf16-rounded gate, as a separate SwiGLU pass over gu would see it
           const float2 gr = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&og[t]));
           const float2 ur = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ou[t]));
-          oh[t] = pack_bf16x2(gr.x / (1.f + __expf(-gr.x)) * ur.x,
-                              gr.y / (1.f + __expf(-gr.y)) * ur.y);
+          // silu(g) = g sigmoid(g) = g (1 + tanh(g / 2)) / 2: one MUFU tanh per element (the
+          // result is rounded to bf16, well above tanh.approx's error)
+          oh[t] = pack_bf16x2(silu_tanh(gr.x) * ur.x, silu_tanh(gr.y) * ur.y);
         }
         __nv_bfloat16* gd = drow + col;
         __nv_bfloat16* ud = drow + p.dual_off + col;
