@@ -7,6 +7,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <tuple>
+
 #include "kernels/launch_api.h"
 
 namespace {
@@ -138,6 +140,17 @@ void gemm_swiglu(const Tensor& x, const Tensor& w, Tensor& gu, Tensor& h) {
                                static_cast<int>(K), err_word(x.get_device()).data_ptr<int>(),
                                cur_stream()),
                "gemm_swiglu");
+}
+
+// (bn, ksplit, pair) the GEMM planner picks for an M x N x K problem on `sms` SMs (host only)
+std::tuple<int64_t, int64_t, bool> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi,
+                                             int64_t bn, int64_t sms) {
+  int obn = 0, oks = 0, opair = 0;
+  CFB_CHECK_RC(cfb_gemm_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                             static_cast<int>(epi), static_cast<int>(bn), static_cast<int>(sms),
+                             &obn, &oks, &opair),
+               "gemm_plan");
+  return {obn, oks, opair != 0};
 }
 
 // dgu [M, 2F] = SwiGLU backward of dh = dy @ wd (wd [H, F], read MN-major) with the gate/up
@@ -651,6 +664,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
   m.def("gemm_swiglu", &gemm_swiglu, "gate/up projection with the SwiGLU epilogue");
+  m.def("gemm_plan", &gemm_plan, "tile / split-K choice of the GEMM planner (host only)");
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd,
         "down-projection dgrad with the SwiGLU backward in the epilogue");
   m.def("gemm_tp", &gemm_tp, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("b_mn"),

@@ -1130,8 +1130,8 @@ struct GemmPlan {
 };
 
 // bn_req: 0 any tile, 128 / 256 that single-CTA tile only, -1 the pair tile only
-static GemmPlan plan_gemm(int M, int N, int K, int bn_req, bool can_split, bool can_pair) {
-  const int sms = num_sms();
+static GemmPlan plan_gemm(int M, int N, int K, int bn_req, bool can_split, bool can_pair,
+                          int sms) {
   const int num_kb = (K + 63) / 64;
   GemmPlan best{256, 1, false};
   double best_t = 1e300;
@@ -1200,7 +1200,8 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
     const bool can_split = epi == kEpiF32Acc && (ldd % 4) == 0 && split_k_on;
     const bool force_pair = bn == kGemmTilePair;
     const bool can_pair = force_pair || (pair_on && bn == 0);
-    const GemmPlan pl = plan_gemm(M, N, K, force_pair ? -1 : bn, can_split, can_pair);
+    const GemmPlan pl =
+        plan_gemm(M, N, K, force_pair ? -1 : bn, can_split, can_pair, num_sms());
     bn = pl.bn;
     ksplit = pl.ksplit;
     pair = pl.pair;
@@ -1357,6 +1358,18 @@ int cfb_gemm_swiglu(const void* A, long long lda, const void* B, long long ldb, 
   }();
   if (pair_on) return launch_gemm_pair<false, false, kEpiSwiGLU>(ta, tb, a, st);
   return launch_gemm<128, false, false, kEpiSwiGLU>(ta, tb, a, st, 0);
+}
+
+int cfb_gemm_plan(int M, int N, int K, int epi, int bn, int sms, int* out_bn, int* out_ksplit,
+                  int* out_pair) {
+  if (M <= 0 || N <= 0 || K <= 0 || sms <= 0) return -10;
+  const bool force_pair = bn == kGemmTilePair;
+  const GemmPlan pl = plan_gemm(M, N, K, force_pair ? -1 : bn, epi == kEpiF32Acc,
+                                force_pair || bn == 0, sms);
+  *out_bn = pl.bn;
+  *out_ksplit = pl.ksplit;
+  *out_pair = pl.pair ? 1 : 0;
+  return 0;
 }
 
 int cfb_gemm_swiglu_bwd(const void* dY, long long ld_dy, const void* Wd, long long ld_w,

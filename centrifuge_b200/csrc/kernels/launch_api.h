@@ -73,6 +73,13 @@ struct CfbTpGemm {
   long long ld_out;
   int out_rows;
 };
+// The tile shape / split-K choice the GEMM entry points make for an M x N x K problem with
+// epilogue `epi` and requested tile `bn` (0, 128, 256, kGemmTilePair) on `sms` SMs (host only;
+// the planner that gemm_entry uses with the device's SM count, ignoring the ldd / environment
+// conditions).
+int cfb_gemm_plan(int M, int N, int K, int epi, int bn, int sms, int* out_bn, int* out_ksplit,
+                  int* out_pair);
+
 int cfb_gemm_tp(const void* A, long long lda, const void* B, long long ldb, int b_mn, void* D,
                 long long ldd, int M, int N, int K, const int* pos, const float* cos_sin,
                 int rope_cols, int head_dim, const CfbTpGemm* tp, int* err, int bn,
