@@ -325,14 +325,21 @@ void swiglu_fwd(const Tensor& gu, Tensor& h) {
 }
 
 void swiglu_bwd(const Tensor& dh, const Tensor& gu, const c10::optional<Tensor>& gu_rows,
-                Tensor& dgu) {
+                Tensor& dgu, const c10::optional<Tensor>& h_out) {
   TORCH_CHECK(dh.is_contiguous() && gu.is_contiguous() && dgu.is_contiguous(), "contiguous");
   const int rows = dh.size(0), F = dh.size(1);
   TORCH_CHECK(dgu.size(0) == rows && dgu.size(1) == 2 * F, "dgu shape");
+  void* hp = nullptr;
+  if (h_out.has_value() && h_out->defined()) {
+    TORCH_CHECK(h_out->is_contiguous() && h_out->size(0) == rows && h_out->size(1) == F &&
+                    h_out->scalar_type() == dh.scalar_type(),
+                "swiglu_bwd: h_out must be [rows, F] like dh");
+    hp = h_out->data_ptr();
+  }
   if (rows == 0) return;
   const c10::cuda::CUDAGuard guard(dh.device());
   CFB_CHECK_RC(cfb_swiglu_bwd(dh.data_ptr(), gu.data_ptr(), opt_ptr<int>(gu_rows), dgu.data_ptr(),
-                              rows, F, cur_stream()),
+                              hp, rows, F, cur_stream()),
                "swiglu_bwd");
 }
 

@@ -297,15 +297,21 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
     load8(gu + r * 2 * F + c, g);
     load8(gu + r * 2 * F + F + c, u);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = g[i] * sigmoidf_(g[i]) * u[i];
+    for (int i = 0; i < 8; ++i) {
+      // the bf16-rounded gate / up as stored, the same formula as the GEMM epilogue
+      o[i] = silu_tanh(g[i]) * u[i];
+    }
     store8(h + r * F + c, o);
   }
 }
 
+// With h_out, also writes h = silu(g) * u of the processed rows (the forward's activation of
+// the kept rows, recomputed instead of gathered).
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh,
                                   const __nv_bfloat16* __restrict__ gu,
                                   const int* __restrict__ gu_rows,
-                                  __nv_bfloat16* __restrict__ dgu, int rows, int F) {
+                                  __nv_bfloat16* __restrict__ dgu,
+                                  __nv_bfloat16* __restrict__ h_out, int rows, int F) {
   const long long groups = static_cast<long long>(rows) * (F / 8);
   for (long long t = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; t < groups;
        t += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -325,6 +331,12 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh,
     }
     store8(dgu + r * 2 * F + c, dg);
     store8(dgu + r * 2 * F + F + c, du);
+    if (h_out) {
+      float h[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = silu_tanh(g[i]) * u[i];
+      store8(h_out + r * F + c, h);
+    }
   }
 }
 
@@ -774,13 +786,13 @@ int cfb_swiglu_fwd(const void* gu, void* h, int rows, int F, cudaStream_t st) {
   return last_err();
 }
 
-int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu, int rows, int F,
-                   cudaStream_t st) {
+int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu, void* h_out,
+                   int rows, int F, cudaStream_t st) {
   if (F % 8) return -11;
   const long long work = static_cast<long long>(rows) * (F / 8);
   swiglu_bwd_kernel<<<grid_for(work, 256, 148 * 32), 256, 0, st>>>(
       static_cast<const bf16*>(dh), static_cast<const bf16*>(gu), gu_rows,
-      static_cast<bf16*>(dgu), rows, F);
+      static_cast<bf16*>(dgu), static_cast<bf16*>(h_out), rows, F);
   return last_err();
 }
 

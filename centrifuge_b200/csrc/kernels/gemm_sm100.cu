@@ -162,13 +162,6 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   tn = r / gsize;
 }
 
-__device__ __forceinline__ float silu_tanh(float g) {
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
-  const float hg = 0.5f * g;
-  return fmaf(hg, t, hg);
-}
-
 // Epilogue of one accumulator row (TMEM lane) of a 128 x BN tile: tcgen05.ld of the fp32
 // accumulator at `taddr` (this warp's lane quadrant), then the EPI-specific conversion and
 // global stores of row `row`, columns [n0, n0 + BN) (clipped to N).

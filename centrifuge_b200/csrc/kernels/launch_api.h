@@ -102,8 +102,8 @@ int cfb_rmsnorm_bwd(const void* dy, const void* x, const int* x_rows, const floa
 int cfb_rope(void* qkv, long long ld, const int* pos, const int* row_of, int rows, int n_heads,
              int head_dim, const float* cos_sin, int inverse, cudaStream_t st);
 int cfb_swiglu_fwd(const void* gu, void* h, int rows, int F, cudaStream_t st);
-int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu, int rows, int F,
-                   cudaStream_t st);
+int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu, void* h_out,
+                   int rows, int F, cudaStream_t st);
 int cfb_gather_rows(const void* src, long long ld_src, const int* idx, void* dst,
                     long long ld_dst, int rows, int row_bytes, cudaStream_t st);
 int cfb_embedding_fwd(const void* table, const long long* ids, void* out, int rows, int H,

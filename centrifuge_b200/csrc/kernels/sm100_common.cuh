@@ -312,6 +312,16 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, b
          | (static_cast<uint32_t>(M >> 4) << 24);  // M / 16
 }
 
+// silu(g) = g sigmoid(g) = g (1 + tanh(g / 2)) / 2 with one hardware tanh (tanh.approx.f32).
+// Every kernel that produces or recomputes the SwiGLU activation uses this one formula, so a
+// recomputed h equals the stored one bit for bit.
+__device__ __forceinline__ float silu_tanh(float g) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(0.5f * g));
+  const float hg = 0.5f * g;
+  return fmaf(hg, t, hg);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);

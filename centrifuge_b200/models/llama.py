@@ -240,14 +240,20 @@ class LlamaCore(torch.nn.Module):
             L = sv.layers[li]
             pre = f"layers.{i}."
             # ---- MLP
-            h_k = self._gather(L["h"], rows)
-            G.linear_wgrad(dx, h_k, g[pre + "wd"])
             dh = G.linear_dgrad(dx, p[pre + "wd"])
-            del h_k
             # a separate pass: the SwiGLU backward in the dgrad epilogue (linear_dgrad_swiglu)
-            # measured slower at these shapes (its gathered gate/up reads stall the epilogue)
-            dgu = fused.swiglu_bwd(dh, L["gu"], rows)
+            # measured slower at these shapes (its gathered gate/up reads stall the epilogue).
+            # The pass also recomputes h of the kept rows from the gate / up it reads anyway,
+            # which replaces a gather of h for the down projection's weight gradient.
+            if rows is None:
+                h_k = L["h"]
+                dgu = fused.swiglu_bwd(dh, L["gu"], None)
+            else:
+                h_k = torch.empty_like(dh)
+                dgu = fused.swiglu_bwd(dh, L["gu"], rows, h_out=h_k)
             del dh
+            G.linear_wgrad(dx, h_k, g[pre + "wd"])
+            del h_k
             xn2_k = self._gather(L["xn2"], rows)
             G.linear_wgrad(dgu, xn2_k, g[pre + "wgu"])
             dxn2 = G.linear_dgrad(dgu, p[pre + "wgu"])

@@ -75,14 +75,20 @@ def swiglu_fwd(gu: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
 
 
 def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor, gu_rows: Optional[torch.Tensor] = None,
-               out: Optional[torch.Tensor] = None) -> torch.Tensor:
+               out: Optional[torch.Tensor] = None,
+               h_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``d[gate; up]`` from ``dh`` and the saved ``gu`` rows ``gu_rows``.  With ``h_out``
+    (``[rows, F]``) the same pass also writes ``h = silu(gate) * up`` of those rows, i.e. the
+    forward activation of the kept rows, recomputed instead of gathered."""
     if out is None:
         out = torch.empty(dh.shape[0], 2 * dh.shape[1], dtype=dh.dtype, device=dh.device)
     if not dh.is_cuda:
         g = gu if gu_rows is None else gu[gu_rows.long()]
         out.copy_(ref.swiglu_bwd(dh, g))
+        if h_out is not None:
+            h_out.copy_(ref.swiglu(g.float()))
         return out
-    kernels().swiglu_bwd(dh, gu, gu_rows, out)
+    kernels().swiglu_bwd(dh, gu, gu_rows, out, h_out)
     return out
 
 

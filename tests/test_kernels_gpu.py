@@ -141,6 +141,18 @@ def test_swiglu():
     dh = torch.randn(rows.numel(), F, device=dev).bfloat16()
     dgu = fused.swiglu_bwd(dh, gu, rows)
     assert rel_err(dgu, ref.swiglu_bwd(dh, gu[rows.long()])) < 1e-2
+    # the kept rows' h recomputed in the backward pass equals the forward's h bit for bit
+    h_k = torch.empty_like(dh)
+    dgu2 = fused.swiglu_bwd(dh, gu, rows, h_out=h_k)
+    assert torch.equal(dgu2, dgu)
+    assert torch.equal(h_k, h[rows.long()])
+    if F % 128 == 0:  # and equals the h of the SwiGLU GEMM epilogue
+        x = torch.randn(T, 256, device=dev).bfloat16()
+        w = (torch.randn(2 * F, 256, device=dev) / 16).bfloat16()
+        gu_g, h_g = gemm.linear_fwd_swiglu(x, w)
+        h_k2 = torch.empty_like(dh)
+        fused.swiglu_bwd(dh, gu_g, rows, h_out=h_k2)
+        assert torch.equal(h_k2, h_g[rows.long()])
 
 
 def test_gather_embedding():
