@@ -37,8 +37,8 @@ if ROOT not in sys.path:
 METRIC = "train tokens/sec (device-timed, max over ranks) @50% filter at 1/2/4/8 B200 vs ref build"
 REFERENCE_UNAVAILABLE = (
     "the reference's grad_filter C++ extension does not compile against the installed torch "
-    "2.11 (Node::add_input_metadata now takes 5 arguments; pip build of /root/reference/"
-    "grad_filter fails in node_processing.cpp:13), and its trainer needs DeepSpeed, which is "
+    "2.11 (Node::add_input_metadata now takes 5 arguments; the pip build of its grad_filter "
+    "package fails in node_processing.cpp:13), and its trainer needs DeepSpeed, which is "
     "not installed")
 
 
