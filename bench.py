@@ -15,6 +15,11 @@ Two measurements, rank 0 prints one JSON line:
   larger than the 126 MB L2.
 * ``e2e``: the same training step through the public API (``Trainer.train_step``) with every
   step's inputs copied host->device from pinned memory and the loss read back to the host.
+
+``--impl reference`` replaces this process by ``baseline/ref_arm.py``: the reference
+implementation's own training step (HF Llama + its ``token_filter_loss`` + its
+``backward_filter_with_dims`` extension) on the same workload, built by
+``baseline/build_ref.sh`` into ``baseline/_ref``.
 """
 from __future__ import annotations
 
@@ -24,7 +29,6 @@ import json
 import os
 import subprocess
 import sys
-import threading
 import time
 
 import torch
@@ -34,12 +38,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
+from baseline.clocks import ClockSampler  # noqa: E402
+
 METRIC = "train tokens/sec (device-timed, max over ranks) @50% filter at 1/2/4/8 B200 vs ref build"
-REFERENCE_UNAVAILABLE = (
-    "the reference's grad_filter C++ extension does not compile against the installed torch "
-    "2.11 (Node::add_input_metadata now takes 5 arguments; the pip build of its grad_filter "
-    "package fails in node_processing.cpp:13), and its trainer needs DeepSpeed, which is "
-    "not installed")
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+REF_ARM = os.path.join(ROOT, "baseline", "ref_arm.py")
 
 
 def parse():
@@ -58,60 +61,11 @@ def parse():
                          "centrifuge: filtered loss and filtered backward")
     ap.add_argument("--zero", type=int, default=2)
     ap.add_argument("--reducer", default="auto", choices=["auto", "nccl", "symm"])
+    ap.add_argument("--layers", type=int, default=None,
+                    help="override the layer count (quick checks only; not a benchmark config)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--json-out", default=None)
     return ap.parse_args()
-
-
-class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons while the timed region runs."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, gpu_index: int):
-        self.idx = gpu_index
-        self.samples = []
-        self._stop = threading.Event()
-        self._th = None
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(
-                    ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                line = out.stdout.strip().splitlines()
-                if line:
-                    self.samples.append([x.strip() for x in line[0].split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
-
-    def __enter__(self):
-        self._th = threading.Thread(target=self._run, daemon=True)
-        self._th.start()
-        return self
-
-    def __exit__(self, *a):
-        self._stop.set()
-        if self._th:
-            self._th.join(timeout=10)
-
-    def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
-        mx = max(float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for s in self.samples:
-            for name, v in zip(names, s[5:9]):
-                if v.strip().lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
 def init_dist(args):
@@ -127,10 +81,32 @@ def init_dist(args):
     return world, rank, local
 
 
+def _reference_built() -> bool:
+    so = os.path.join(REF_DIR, "grad_filter", "token_filter")
+    return os.path.isdir(so) and any(f.startswith("_C") and f.endswith(".so") for f in os.listdir(so))
+
+
 def run_reference(args):
-    line = {"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}
-    if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps(line), flush=True)
+    """Replace this process by the reference arm (baseline/ref_arm.py), which runs the
+    reference's own training step; build the reference first if baseline/_ref is missing."""
+    rank = int(os.environ.get("RANK", "0"))
+    if not _reference_built() and rank == 0:
+        subprocess.run(["bash", os.path.join(ROOT, "baseline", "build_ref.sh")], check=False)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # every rank waits for rank 0's build through the filesystem (no process group yet)
+        for _ in range(600):
+            if _reference_built():
+                break
+            time.sleep(1)
+    if not _reference_built():
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable":
+                              "the reference's grad_filter extension is not built and "
+                              "baseline/build_ref.sh could not build it here"}), flush=True)
+        return
+    argv = [sys.executable, REF_ARM] + sys.argv[1:]
+    sys.stdout.flush()
+    os.execv(sys.executable, argv)
 
 
 def main():
@@ -151,6 +127,8 @@ def main():
     dev = torch.device("cuda", local)
     cfg = get_model_config(args.model)
     cfg.max_position_embeddings = max(cfg.max_position_embeddings, args.seq)
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
     model = NativeLlamaForCausalLM(cfg, device=dev, seed=4321, pad_to=world)
     group = dist.group.WORLD if world > 1 else None
     reducer = None
@@ -233,6 +211,7 @@ def main():
                        "micro_batch": args.mbs, "grad_accum": args.ga, "seq_len": args.seq,
                        "drop_rate": drop, "mode": args.mode,
                        "parallelism": f"zero{args.zero}-dp{world}",
+                       "layers": cfg.num_hidden_layers,
                        "reducer": (getattr(opt.reducer, "kind", type(opt.reducer).__name__)
                                    if opt.reducer else "none"),
                        "l2": "working set (weights + activations) far larger than L2"},
