@@ -32,12 +32,23 @@ inline const T* opt_ptr(const c10::optional<Tensor>& t) {
   return (t.has_value() && t->defined()) ? static_cast<const T*>(t->data_ptr()) : nullptr;
 }
 
+// Per-device status block handed to every kernel as `err` (layout in sm100_common.cuh):
+// [0] first error code, [1] local wait limit (us, 0 = default), [2] peer wait limit (us),
+// [3] reserved.
+constexpr int64_t kStatusWordsHost = 4;
 Tensor& err_word(int device) {
   static std::vector<Tensor> words(64);
   Tensor& w = words.at(device);
   if (!w.defined())
-    w = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
+    w = at::zeros({kStatusWordsHost},
+                  at::TensorOptions().dtype(at::kInt).device(at::kCUDA, device));
   return w;
+}
+
+inline void check_status(const Tensor& err, const char* what) {
+  TORCH_CHECK(err.is_cuda() && err.scalar_type() == at::kInt && err.is_contiguous() &&
+                  err.numel() >= kStatusWordsHost,
+              what, ": err must be a device status block (int32, >= 4 words; see status_block)");
 }
 
 // Work counter of the persistent attention kernels (two int32 words per device, zero at rest;
@@ -257,9 +268,22 @@ void gemm_tp(const Tensor& a, const Tensor& b, Tensor& out, bool b_mn,
 
 int64_t gemm_error_word(int64_t device, bool reset) {
   Tensor& w = err_word(static_cast<int>(device));
-  const int64_t v = w.item<int>();
-  if (reset) w.zero_();
+  const int64_t v = w[0].item<int>();
+  if (reset) w[0].zero_();
   return v;
+}
+
+// The device status block itself (shared by every kernel launched on `device`).
+Tensor status_block(int64_t device) { return err_word(static_cast<int>(device)); }
+
+// Limits of the bounded device waits on `device`, in microseconds (0 restores the default:
+// 4 s for waits on the GPU's own work, 20 s for waits on another GPU).  Stream-ordered.
+void set_wait_limits(int64_t device, int64_t local_us, int64_t peer_us) {
+  TORCH_CHECK(local_us >= 0 && local_us <= INT32_MAX && peer_us >= 0 && peer_us <= INT32_MAX,
+              "set_wait_limits: limits must be in [0, 2^31) microseconds");
+  Tensor& w = err_word(static_cast<int>(device));
+  w[1].fill_(local_us);
+  w[2].fill_(peer_us);
 }
 
 void rmsnorm_fwd(const Tensor& x, const Tensor& w, Tensor& y, const c10::optional<Tensor>& rstd,
@@ -468,7 +492,8 @@ void clip_coef(const Tensor& partials, double max_norm, double extra_scale, Tens
                Tensor& norm) {
   const c10::cuda::CUDAGuard guard(partials.device());
   CFB_CHECK_RC(cfb_clip_coef(partials.data_ptr<float>(), partials.numel(), max_norm, extra_scale,
-                             coef.data_ptr<float>(), norm.data_ptr<float>(), cur_stream()),
+                             coef.data_ptr<float>(), norm.data_ptr<float>(),
+                             err_word(partials.get_device()).data_ptr<int>(), cur_stream()),
                "clip_coef");
 }
 
@@ -496,6 +521,7 @@ void keep_index(const Tensor& mask, int64_t S_keep, Tensor& pos, Tensor& flat_ro
   TORCH_CHECK(mask.scalar_type() == at::kLong && mask.is_contiguous() && mask.dim() == 2,
               "mask int64 [B, S]");
   TORCH_CHECK(pos.scalar_type() == at::kInt && flat_rows.scalar_type() == at::kInt, "int32");
+  check_status(err, "keep_index");
   const c10::cuda::CUDAGuard guard(mask.device());
   CFB_CHECK_RC(cfb_keep_index(reinterpret_cast<const long long*>(mask.data_ptr<int64_t>()),
                               mask.size(0), mask.size(1), S_keep, pos.data_ptr<int>(),
@@ -613,6 +639,7 @@ void symm_signal(int64_t peer_flags_dev, int64_t W, int64_t off, int64_t epoch) 
 
 void symm_wait(int64_t flags, int64_t base, int64_t stride, int64_t n, int64_t epoch,
                Tensor& err) {
+  check_status(err, "symm_wait");
   CFB_CHECK_RC(cfb_symm_wait(reinterpret_cast<const uint32_t*>(flags), base, stride, n,
                              static_cast<uint32_t>(epoch), err.data_ptr<int>(), cur_stream()),
                "symm_wait");
@@ -622,11 +649,23 @@ void symm_pull_reduce(int64_t mc_base, int64_t peer_base_dev, int64_t W, int64_t
                       Tensor& dst, double scale, Tensor& err) {
   TORCH_CHECK(dst.scalar_type() == at::kFloat && dst.is_contiguous() && dst.numel() == n,
               "symm_pull_reduce: dst must be a contiguous fp32 [n] tensor");
+  check_status(err, "symm_pull_reduce");
   CFB_CHECK_RC(cfb_symm_pull_reduce(reinterpret_cast<const float*>(mc_base),
                                     reinterpret_cast<const float* const*>(peer_base_dev), W, off,
                                     n, dst.data_ptr<float>(), static_cast<float>(scale), nullptr,
                                     0, 0, err.data_ptr<int>(), cur_stream()),
                "symm_pull_reduce");
+}
+
+// buf = 0 unless err[0] != 0 (a failed peer wait: a peer may still be reading buf)
+void zero_unless_error(Tensor& buf, const Tensor& err) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(),
+              "zero_unless_error: contiguous fp32 CUDA buffer");
+  check_status(err, "zero_unless_error");
+  const c10::cuda::CUDAGuard guard(buf.device());
+  CFB_CHECK_RC(cfb_zero_unless_error(buf.data_ptr<float>(), buf.numel(), err.data_ptr<int>(),
+                                     cur_stream()),
+               "zero_unless_error");
 }
 
 // Dispatcher-visible attention ops on token-major rows, used by the graph rewriter's filtered
@@ -670,6 +709,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a_mn"), py::arg("b_mn"), py::arg("epi"), py::arg("resid") = py::none(),
         py::arg("alpha") = 1.0, py::arg("bn") = 0, py::arg("max_ctas") = 0);
   m.def("gemm_error_word", &gemm_error_word, py::arg("device") = 0, py::arg("reset") = true);
+  m.def("status_block", &status_block, "per-device status block of the kernels",
+        py::arg("device") = 0);
+  m.def("set_wait_limits", &set_wait_limits, py::arg("device"), py::arg("local_us"),
+        py::arg("peer_us"));
+  m.def("zero_unless_error", &zero_unless_error);
   m.def("gemm_swiglu", &gemm_swiglu, "gate/up projection with the SwiGLU epilogue");
   m.def("gemm_plan", &gemm_plan, "tile / split-K choice of the GEMM planner (host only)");
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd,

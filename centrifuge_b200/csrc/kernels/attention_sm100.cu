@@ -141,7 +141,7 @@ __device__ __forceinline__ bool group_exchange(float* vals, volatile int* flags,
     while (flags[q * BMr + r] < seq) {
       if ((++spins & 255u) == 0) {
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > local_wait_limit_ns(err)) {
           *abort_flag = 1;
           atomicCAS(err, 0, kErrWaitSoftmax);
           return false;

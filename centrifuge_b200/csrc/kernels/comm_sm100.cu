@@ -14,15 +14,16 @@
 //   3. micro-batch done: after its last bucket each rank stores `epoch` into done[me] of every
 //      peer and waits (bounded) for done[p] >= epoch of all peers before its gradient buffer is
 //      cleared for the next micro-batch.
-// Waits give up after a time limit and record an error code in a device word that the host
-// reads; they never trap.  No TMA is used here.
+// Waits give up after the peer wait limit of the status block (err[2], default 20 s) and record
+// kErrPeerWait in err[0], which the host reads one step later; they never trap.  Every kernel
+// after a failed wait sees err[0] != 0 and skips its work: the pull does not sum half-written
+// peer buffers, and the local gradient buffer is not cleared while a peer may still read it.
+// No TMA is used here.
 #include "sm100_common.cuh"
 #include "launch_api.h"
 
 namespace cfb {
 namespace comm {
-
-constexpr uint64_t kFlagWaitNs = 20000000000ull;  // 20 s
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -45,11 +46,12 @@ __device__ __forceinline__ float4 multimem_ld_reduce_add_v4(const float* mc) {
 __device__ bool wait_flags(const uint32_t* flags, int base, int stride, int n, uint32_t epoch,
                            int* err, int code) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = peer_wait_limit_ns(err);
   for (int i = 0; i < n; ++i) {
     const uint32_t* f = flags + base + i * stride;
     uint32_t spins = 0;
     while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
-      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kFlagWaitNs) {
+      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > limit) {
         atomicCAS(err, 0, code);
         return false;
       }
@@ -83,6 +85,8 @@ __global__ void __launch_bounds__(512) pull_reduce_kernel(
       ok = wait_flags(flags, bucket * W, 1, W, epoch, err, kErrPeerWait) ? 1 : 0;
     __syncthreads();
     if (!ok) return;
+  } else if (*reinterpret_cast<volatile int*>(err) != 0) {
+    return;  // an earlier wait of this step gave up: peer buffers may be half written
   }
   const long long n4 = n / 4;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
@@ -107,6 +111,20 @@ __global__ void __launch_bounds__(512) pull_reduce_kernel(
     d.w += scale * s.w;
     reinterpret_cast<float4*>(dst)[i] = d;
   }
+}
+
+// buf[0, n) = 0 unless err[0] != 0 (then a peer may still be reading the buffer: keep it)
+__global__ void __launch_bounds__(512) zero_unless_error_kernel(float* __restrict__ buf,
+                                                                long long n, const int* err) {
+  if (*reinterpret_cast<const volatile int*>(err) != 0) return;
+  const long long n4 = n / 4;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += stride)
+    reinterpret_cast<float4*>(buf)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long i = 4 * n4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+       i < n; i += stride)
+    buf[i] = 0.f;
 }
 
 }  // namespace comm
@@ -137,5 +155,15 @@ int cfb_symm_pull_reduce(const float* mc_base, const float* const* peer_base_dev
   if (blocks > 148 * 4) blocks = 148 * 4;
   pull_reduce_kernel<<<static_cast<int>(blocks), 512, 0, st>>>(
       mc_base, peer_base_dev, W, off, n, dst, scale, flags, bucket, epoch, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int cfb_zero_unless_error(float* buf, long long n, const int* err, cudaStream_t st) {
+  if (n <= 0) return 0;
+  if ((reinterpret_cast<uintptr_t>(buf) & 15) != 0) return -11;
+  long long blocks = (n / 4 + 511) / 512;
+  if (blocks > 148 * 4) blocks = 148 * 4;
+  if (blocks < 1) blocks = 1;
+  zero_unless_error_kernel<<<static_cast<int>(blocks), 512, 0, st>>>(buf, n, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

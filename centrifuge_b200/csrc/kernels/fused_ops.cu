@@ -521,6 +521,7 @@ __global__ void adamw_kernel(float* __restrict__ master, const float* __restrict
                              float b1, float b2, float eps, float wd, float bc1, float bc2,
                              const float* __restrict__ grad_scale) {
   const float gs = grad_scale ? *grad_scale : 1.f;
+  if (gs < 0.f) return;  // clip_coef marked the step as failed: no update
   const float step_size = lr / bc1;
   const float inv_sqrt_bc2 = rsqrtf(bc2);
   const long long n4 = n / 4;
@@ -591,9 +592,11 @@ __global__ void sumsq_kernel(const float* __restrict__ x, long long n, float* __
 }
 
 // coef = min(1, max_norm / (norm + 1e-6)) * extra_scale  (max_norm <= 0: no clipping)
+// status[0] != 0 (a bounded wait of this step gave up): coef = -1, the AdamW kernels' signal to
+// leave parameters and moments untouched.
 __global__ void clip_coef_kernel(const float* __restrict__ partials, int n, float max_norm,
                                  float extra_scale, float* __restrict__ coef,
-                                 float* __restrict__ norm_out) {
+                                 float* __restrict__ norm_out, const int* status) {
   __shared__ float red[32];
   float s = 0.f;
   for (int i = threadIdx.x; i < n; i += blockDim.x) s += partials[i];
@@ -608,7 +611,8 @@ __global__ void clip_coef_kernel(const float* __restrict__ partials, int n, floa
       const float norm = sqrtf(s) * extra_scale;
       float c = 1.f;
       if (max_norm > 0.f && norm > max_norm) c = max_norm / (norm + 1e-6f);
-      if (coef) *coef = c * extra_scale;
+      const bool failed = status != nullptr && *reinterpret_cast<const volatile int*>(status) != 0;
+      if (coef) *coef = failed ? -1.f : c * extra_scale;
       if (norm_out) *norm_out = norm;
     }
   }
@@ -699,7 +703,7 @@ __global__ void __launch_bounds__(1024) keep_index_kernel(const long long* __res
     __syncthreads();
   }
   const int total = counts[blockDim.x - 1];
-  if (threadIdx.x == 0 && total != S_keep && err) atomicExch(err, 1);
+  if (threadIdx.x == 0 && total != S_keep && err) atomicCAS(err, 0, kErrKeepCount);
   int j = counts[threadIdx.x] - c;
   for (int s = s0; s < s1; ++s) {
     if (mr[s] != 0) {
@@ -878,8 +882,8 @@ int cfb_sumsq(const float* x, long long n, float* out_partial, int nblocks, cuda
 }
 
 int cfb_clip_coef(const float* partials, int n, float max_norm, float extra_scale, float* coef,
-                  float* norm_out, cudaStream_t st) {
-  clip_coef_kernel<<<1, 256, 0, st>>>(partials, n, max_norm, extra_scale, coef, norm_out);
+                  float* norm_out, const int* status, cudaStream_t st) {
+  clip_coef_kernel<<<1, 256, 0, st>>>(partials, n, max_norm, extra_scale, coef, norm_out, status);
   return last_err();
 }
 

@@ -88,7 +88,6 @@ struct GemmArgs {
 };
 
 namespace tpc {
-constexpr uint64_t kPeerWaitNs = 20000000000ull;  // 20 s
 __device__ __forceinline__ uint4 ld_reduce_bf16x8(const __nv_bfloat16* mc) {
   uint4 r;
   asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
@@ -110,12 +109,13 @@ __device__ __forceinline__ void st_release_sys(uint32_t* f, uint32_t v) {
 __device__ __forceinline__ bool wait_epoch(const uint32_t* flags, int n, uint32_t epoch,
                                            volatile int* abort, int* err) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = peer_wait_limit_ns(err);
   for (int i = 0; i < n; ++i) {
     uint32_t spins = 0;
     while (static_cast<int32_t>(ld_acquire_sys(flags + i) - epoch) < 0) {
       if ((++spins & 255u) == 0) {
         if (*abort) return false;
-        if (globaltimer_ns() - t0 > kPeerWaitNs) {
+        if (globaltimer_ns() - t0 > limit) {
           *abort = 1;
           atomicCAS(err, 0, kErrPeerWait);
           return false;

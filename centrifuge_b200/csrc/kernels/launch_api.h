@@ -127,8 +127,10 @@ int cfb_adamw_multicast(float* master, const float* grad, float* m, float* v, vo
                         long long n, float lr, float beta1, float beta2, float eps, float wd,
                         float bc1, float bc2, const float* grad_scale, cudaStream_t st);
 int cfb_sumsq(const float* x, long long n, float* out_partial, int nblocks, cudaStream_t st);
+// coef = min(1, max_norm / norm) * extra_scale; when status[0] != 0 (a wait of this step gave
+// up) coef = -1, which makes the AdamW kernels skip the update.
 int cfb_clip_coef(const float* partials, int n, float max_norm, float extra_scale, float* coef,
-                  float* norm_out, cudaStream_t st);
+                  float* norm_out, const int* status, cudaStream_t st);
 int cfb_drop_smallest(const float* score, long long ld, int* mask_i32, long long* mask_i64,
                       long long ld_mask, int rows, int start, int end, int k, cudaStream_t st);
 int cfb_keep_index(const long long* mask, int B, int S, int S_keep, int* pos, int* flat_rows,
@@ -173,3 +175,5 @@ int cfb_symm_pull_reduce(const float* mc_base, const float* const* peer_base_dev
                          long long off, long long n, float* dst, float scale,
                          const uint32_t* flags, int bucket, uint32_t epoch, int* err,
                          cudaStream_t st);
+// buf[0, n) = 0 unless err[0] != 0 (buf 16-byte aligned)
+int cfb_zero_unless_error(float* buf, long long n, const int* err, cudaStream_t st);

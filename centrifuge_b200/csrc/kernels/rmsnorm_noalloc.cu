@@ -156,8 +156,18 @@ extern "C" int cfb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const int*
                                        cudaStream_t stream) {
   if (!dy || !x || !rstd || !w || !dx || !dw_acc || rows < 0 || H <= 0 || (H % 8) != 0)
     return CFB_NOALLOC_ERR_BAD_ARGS;
+  // the kernels move 8 bf16 values (16 bytes) per access of dy, x, w, dres and dx
+  const auto misaligned = [](const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) != 0;
+  };
+  if (misaligned(dy) || misaligned(x) || misaligned(w) || misaligned(dx) ||
+      (dres != nullptr && misaligned(dres)))
+    return CFB_NOALLOC_ERR_BAD_ARGS;
   if (H > 8192) return CFB_NOALLOC_ERR_TOO_LARGE;
   if (rows == 0) return CFB_NOALLOC_OK;
+  // An error left pending by earlier work on this thread belongs to its owner: report it
+  // without launching and without clearing it.
+  if (cudaPeekAtLastError() != cudaSuccess) return CFB_NOALLOC_ERR_PENDING;
   int err = CFB_NOALLOC_OK;
   float* scratch = scratch_for_current_device(&err);
   if (scratch == nullptr) return err;
@@ -178,18 +188,25 @@ extern "C" int cfb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const int*
     case 3: rms_bwd_partial<3><<<P, 256, 0, stream>>>(a, b, x_rows, rstd, c, d, o, scratch, rows, H); break;
     default: rms_bwd_partial<4><<<P, 256, 0, stream>>>(a, b, x_rows, rstd, c, d, o, scratch, rows, H); break;
   }
+  if (cudaGetLastError() != cudaSuccess) return CFB_NOALLOC_ERR_LAUNCH;
   rms_bwd_colsum<<<(H + 255) / 256, 256, 0, stream>>>(scratch, dw_acc, P, H);
-  return cudaGetLastError() == cudaSuccess ? CFB_NOALLOC_OK : CFB_NOALLOC_ERR_LAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return CFB_NOALLOC_ERR_LAUNCH;
+  return CFB_NOALLOC_OK;
 }
 
 extern "C" const char* cfb_noalloc_strerror(int code) {
   switch (code) {
     case CFB_NOALLOC_OK: return "ok";
-    case CFB_NOALLOC_ERR_BAD_ARGS: return "bad arguments (null pointer, negative size or H % 8 != 0)";
+    case CFB_NOALLOC_ERR_BAD_ARGS:
+      return "bad arguments (null pointer, negative size, H % 8 != 0, or a bf16 buffer not "
+             "16-byte aligned)";
     case CFB_NOALLOC_ERR_TOO_LARGE:
       return "hidden size beyond the fixed scratch limit (H must be <= 8192)";
     case CFB_NOALLOC_ERR_SYMBOL: return "could not resolve the device scratch address";
     case CFB_NOALLOC_ERR_LAUNCH: return "kernel launch failed";
+    case CFB_NOALLOC_ERR_PENDING:
+      return "an earlier CUDA error is pending on this thread (left for its owner; nothing "
+             "launched)";
   }
   return "unknown error";
 }

@@ -13,7 +13,11 @@
 //   dw_acc   += sum_r dy[r] * x[x_rows[r]] * rstd[x_rows[r]]         (fp32, [H])
 //
 // Same semantics and argument meaning as cfb_rmsnorm_bwd (launch_api.h); x_rows and dres may be
-// null.  Limits: H % 8 == 0, H <= 8192, and at most CFB_NOALLOC_SCRATCH_FLOATS fp32 scratch
+// null.  dy, x, w, dres and dx are read and written 16 bytes at a time, so each must start on a
+// 16-byte boundary (otherwise CFB_NOALLOC_ERR_BAD_ARGS).  If an earlier CUDA error is pending on
+// the calling thread, the call launches nothing, leaves that error in place for its owner and
+// returns CFB_NOALLOC_ERR_PENDING.
+// Limits: H % 8 == 0, H <= 8192, and at most CFB_NOALLOC_SCRATCH_FLOATS fp32 scratch
 // elements (4 MiB), which this entry point never exceeds for H <= 8192 by using fewer partial
 // rows; larger H is rejected with CFB_NOALLOC_ERR_TOO_LARGE.
 //
@@ -34,6 +38,7 @@ enum {
   CFB_NOALLOC_ERR_TOO_LARGE = -2,
   CFB_NOALLOC_ERR_SYMBOL = -3,
   CFB_NOALLOC_ERR_LAUNCH = -4,
+  CFB_NOALLOC_ERR_PENDING = -5,
 };
 
 #ifdef __cplusplus

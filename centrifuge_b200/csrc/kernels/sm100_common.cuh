@@ -12,7 +12,14 @@
 
 namespace cfb {
 
-// Error codes written to the per-launch error word when a bounded wait gives up.
+// Every kernel that can fail on the device receives `err`, the base of the per-device status
+// block (int32 words, zero-initialised, owned by the host bindings):
+//   err[0]  first error code (kErr*), set with atomicCAS(err, 0, code); the host reads it
+//   err[1]  limit of a wait on this GPU's own work (mbarriers), microseconds; 0 = kWaitLimitNs
+//   err[2]  limit of a wait on another GPU (peer flags), microseconds; 0 = kPeerWaitLimitNs
+//   err[3]  reserved
+// The limits are read at run time, so the host can shorten them (tests make a wait on a flag
+// that nothing raises run out in milliseconds) without rebuilding.
 enum : int {
   kErrNone = 0,
   kErrWaitProducer = 1,
@@ -21,10 +28,25 @@ enum : int {
   kErrWaitSoftmax = 4,
   kErrBadArgs = 16,
   kErrPeerWait = 32,
+  kErrKeepCount = 64,
 };
+constexpr int kStatusWords = 4;
 
-// A bounded wait gives up after this many nanoseconds of %globaltimer.
-constexpr uint64_t kWaitLimitNs = 4000000000ull;
+// Default limits of the bounded waits (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitLimitNs = 4000000000ull;       // 4 s
+constexpr uint64_t kPeerWaitLimitNs = 20000000000ull;  // 20 s
+
+__device__ __forceinline__ uint64_t status_limit_ns(const int* err, int word, uint64_t dflt) {
+  if (err == nullptr) return dflt;
+  const int us = *reinterpret_cast<const volatile int*>(err + word);
+  return us > 0 ? static_cast<uint64_t>(us) * 1000ull : dflt;
+}
+__device__ __forceinline__ uint64_t local_wait_limit_ns(const int* err) {
+  return status_limit_ns(err, 1, kWaitLimitNs);
+}
+__device__ __forceinline__ uint64_t peer_wait_limit_ns(const int* err) {
+  return status_limit_ns(err, 2, kPeerWaitLimitNs);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -72,11 +94,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = local_wait_limit_ns(err);
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit) {
         *abort = 1;
         if (err) atomicCAS(err, 0, code);
         return false;

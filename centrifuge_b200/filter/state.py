@@ -42,9 +42,14 @@ class FilterState:
         return self.B * self.s_keep
 
     def check(self):
-        """Raise if a row did not keep ``s_keep`` tokens (host sync; used by tests/debug)."""
-        if int(self.err.item()) != 0:
-            raise ValueError(f"mask rows do not all keep {self.s_keep} tokens")
+        """Raise if a row did not keep ``s_keep`` tokens (host sync; used by tests/debug).
+
+        On the GPU this reads the device status block, which also collects the other kernels'
+        errors; the training loop reads it asynchronously instead (``DeviceStatus``)."""
+        code = int(self.err.reshape(-1)[0].item())
+        if code != 0:
+            self.err.reshape(-1)[:1].zero_()
+            raise ValueError(f"mask rows do not all keep {self.s_keep} tokens (device code {code})")
 
 
 def state_for_mask(mask: torch.Tensor) -> FilterState:

@@ -128,6 +128,9 @@ def _drop_smallest(score: torch.Tensor, attention_mask: torch.Tensor, rate: floa
         n = S - 1
         k = int(rate * n)
         start, end = (0, S - 1) if left_padding else (1, S)
+        # the score has S-1 columns: right padding's range [1, S) is [1, S-1) in effect, as
+        # the reference's slice loss_diff[i][1:S] truncates it (model/utils.py:418)
+        end = min(end, int(score.shape[1]))
         if k <= 0:
             return attention_mask
         if attention_mask.is_cuda and k < end - start:

@@ -23,9 +23,11 @@ def drop_smallest_(score: torch.Tensor, mask: torch.Tensor, k: int, start: int, 
 
 
 def keep_index(mask: torch.Tensor, s_keep: int):
-    """``(pos [B, S_keep] int32, flat_rows [B*S_keep] int32, err [1] int32)``.
+    """``(pos [B, S_keep] int32, flat_rows [B*S_keep] int32, status)``.
 
-    ``err`` is non-zero on the device when a row does not keep exactly ``s_keep`` tokens.
+    On the GPU ``status`` is the kernels' per-device status block; its word 0 becomes
+    ``kErrKeepCount`` (64) when a row does not keep exactly ``s_keep`` tokens (the training loop
+    reads it one step late).  On the CPU a wrong count raises at once.
     """
     B, S = mask.shape
     if not mask.is_cuda:
@@ -40,6 +42,6 @@ def keep_index(mask: torch.Tensor, s_keep: int):
     m = m.contiguous()
     pos = torch.empty(B, s_keep, dtype=torch.int32, device=mask.device)
     flat = torch.empty(B * s_keep, dtype=torch.int32, device=mask.device)
-    err = torch.zeros(1, dtype=torch.int32, device=mask.device)
+    err = kernels().status_block(mask.device.index)
     kernels().keep_index(m, s_keep, pos, flat, err)
     return pos, flat, err

@@ -65,13 +65,19 @@ class PipelineTrainer:
     """1F1B training step of one pipeline stage (this process)."""
 
     def __init__(self, core, optimizer, groups: PPGroups, drop_rate: float = 0.5,
-                 strategy: str = "fixed", num_microbatches: int = 8):
+                 strategy: str = "fixed", num_microbatches: int = 8,
+                 check_device_errors: bool = True):
         self.core, self.opt, self.g = core, optimizer, groups
         self.drop_rate, self.strategy, self.M = drop_rate, strategy, num_microbatches
         self.first = groups.stage == 0
         self.last = groups.stage == groups.pp - 1
         self.device = core.device
         self._sends: List = []
+        # device errors (bounded waits that ran out, bad masks) surface one step late
+        self.status = None
+        if check_device_errors and torch.device(self.device).type == "cuda":
+            from ..utils.device_status import DeviceStatus
+            self.status = DeviceStatus(self.device)
 
     # ------------------------------------------------------------------ p2p
     def _isend(self, t: torch.Tensor, dst: int) -> None:
@@ -122,6 +128,9 @@ class PipelineTrainer:
         else:
             mask = self._recv((B, S), torch.long, self.g.next)
             filtered = bool(self.drop_rate > 0)
+            if filtered and self.strategy == "fixed":
+                # every row keeps S - k tokens, known statically: no host read of the mask
+                mask._cf_keep = keep_count(S, self.drop_rate)
             state = state_for_mask(mask) if filtered else None
             lay = KeptLayout(state.rows if state is not None else None, B * S,
                              self.core.tp, self.device)
@@ -162,4 +171,6 @@ class PipelineTrainer:
         self.core.reduce_replicated_grads()
         self.opt.step(grad_scale=1.0 / M)
         self.opt.zero_grad()
+        if self.status is not None:
+            self.status.record()
         return torch.stack(losses).mean() if losses else None

@@ -10,8 +10,10 @@ kernel on this path; gradients travel as fp32 so the accumulation is exact.
 
 Ordering uses per-bucket "ready" flags and a per-micro-batch "done" flag in a small
 symmetric flag buffer, written with release stores and waited on with bounded acquire spins
-(timeout -> error word, never a trap).  The local gradient buffer is cleared only after every
-rank has finished reading it.
+(timeout -> the device status block's error word, never a trap).  The local gradient buffer is
+cleared only after every rank has finished reading it; after a failed wait the pull and the
+clear are skipped on the device and the step's AdamW update too (the trainer's
+:class:`~centrifuge_b200.utils.device_status.DeviceStatus` raises one step later).
 """
 from __future__ import annotations
 
@@ -53,7 +55,8 @@ class SymmReducer:
         self.flags.zero_()
         self.fhdl = symm_mem.rendezvous(self.flags, group)
         self.peer_flags_dev = int(self.fhdl.buffer_ptrs_dev)
-        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        # the kernels' per-device status block (error word + wait limits)
+        self.err = kernels().status_block(dev.index)
         self.epoch = 1
         self.base_ptr = buf.data_ptr()
         torch.cuda.synchronize(dev)
@@ -80,7 +83,7 @@ class SymmReducer:
         base = MAX_BUCKETS * self.W
         k.symm_signal(self.peer_flags_dev, self.W, base + self.rank, self.epoch)
         k.symm_wait(self.flags.data_ptr(), base, 1, self.W, self.epoch, self.err)
-        flat.grad.zero_()
+        k.zero_unless_error(flat.grad, self.err)
         self.epoch += 1
 
     def adamw_all_gather(self, opt, coef: torch.Tensor) -> None:
@@ -106,6 +109,8 @@ class SymmReducer:
 
     def check(self) -> None:
         """Raise if a peer wait timed out (reads the device error word: host sync)."""
-        v = int(self.err.item())
+        v = int(self.err[0].item())
         if v:
-            raise RuntimeError(f"symmetric-memory reduction: peer wait timed out (code {v})")
+            from ..utils.device_status import DeviceError
+            self.err[:1].zero_()
+            raise DeviceError(v)

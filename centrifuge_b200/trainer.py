@@ -4,7 +4,8 @@ Per micro-batch: forward (fused lm_head + per-token CE), utility-based token sel
 (``token_filter_loss``), ``backward_filter`` on the loss, the filtered backward (gradients
 reduced on the fly by the ZeRO optimizer), and after ``grad_accum`` micro-batches one fused
 AdamW step.  Mirrors ``Trainer.train_step`` of the reference (train.py:222-326) without its
-host synchronisations: the only device-to-host read is the optional loss readout.
+host synchronisations: the only device-to-host reads are the optional loss readout and the
+asynchronous copy of the kernels' status word, checked one step late.
 """
 from __future__ import annotations
 
@@ -20,7 +21,7 @@ from .loss import keep_count, token_filter_loss
 class Trainer:
     def __init__(self, model, optimizer, drop_rate: float = 0.5, strategy: str = "fixed",
                  grad_accum: int = 1, world_size: int = 1, timer=None,
-                 filter_backward: bool = True):
+                 filter_backward: bool = True, check_device_errors: bool = True):
         self.model = model
         self.opt = optimizer
         self.drop_rate = drop_rate
@@ -33,6 +34,13 @@ class Trainer:
         self.device = model.device
         if hasattr(optimizer, "attach"):
             optimizer.attach(model)
+        # Device errors (a bounded wait that ran out, a mask row with the wrong keep count) are
+        # read one step late from the kernels' status block; the failed step's AdamW update is
+        # already skipped on the device.  Raises DeviceError.
+        self.status = None
+        if check_device_errors and torch.device(self.device).type == "cuda":
+            from .utils.device_status import DeviceStatus
+            self.status = DeviceStatus(self.device)
 
     def micro_step(self, batch: Batch, last: bool = True) -> torch.Tensor:
         """Forward + filtered backward of one micro-batch; ``last`` marks the last micro-batch
@@ -70,4 +78,6 @@ class Trainer:
             total += self.micro_step(b, last=(i == len(batches) - 1))
         self.opt.step(grad_scale=1.0 / (self.grad_accum * self.world))
         self.opt.zero_grad()
+        if self.status is not None:
+            self.status.record()
         return total / self.grad_accum

@@ -230,9 +230,26 @@ def test_drop_smallest_and_keep_index(S, drop):
     want.scatter_(1, idx, 0)
     assert torch.equal(mask.cpu(), want)
     pos, flat, err = select.keep_index(mask, S - k)
-    assert err.item() == 0
+    assert int(err[0]) == 0
     pos_c, flat_c, _ = select.keep_index(want, S - k)
     assert torch.equal(pos.cpu(), pos_c) and torch.equal(flat.cpu(), flat_c)
+
+
+@pytest.mark.parametrize("left", [True, False])
+def test_token_dropping_mask_full_rows_cpu_vs_cuda(left):
+    """Full rows with either padding side: the device selection agrees with the CPU path (right
+    padding's range [1, S) is truncated to the S-1 loss columns, as the reference's slice is)."""
+    from centrifuge_b200.loss import token_dropping_mask
+    torch.manual_seed(11)
+    B, S = 3, 300
+    loss = torch.randn(B, S - 1)
+    ref = torch.randn(B, S - 1)
+    m_cpu = token_dropping_mask(loss, ref, torch.ones(B, S, dtype=torch.long), "fixed", 0.5,
+                                left_padding=left)
+    m_gpu = token_dropping_mask(loss.to(dev), ref.to(dev),
+                                torch.ones(B, S, dtype=torch.long, device=dev), "fixed", 0.5,
+                                left_padding=left)
+    assert torch.equal(m_gpu.cpu(), m_cpu)
 
 
 @pytest.mark.parametrize("B,S,nh,nkv,hd", [(2, 256, 4, 2, 64), (1, 200, 4, 1, 128),
