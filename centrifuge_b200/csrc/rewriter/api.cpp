@@ -190,7 +190,69 @@ TORCH_LIBRARY(token_filter, m) {
   m.def("collect_node_names(Tensor loss) -> str[]");
 }
 
-TORCH_LIBRARY_IMPL(token_filter, CompositeImplicitAutograd, m) {
+namespace cfb_filter {
+namespace {
+
+// Tensors of a tracer (FakeTensor and other Python-dispatched tensors, meta tensors) have no
+// autograd graph to rewrite: their calls go below autograd to the fake kernels registered from
+// Python (centrifuge_b200.filter), which is what torch.compile's tracing sees.
+bool traced(const at::Tensor& t) {
+  return t.defined() && (t.is_meta() || t.key_set().has(c10::DispatchKey::Python));
+}
+
+c10::OperatorHandle op_handle(const char* name) {
+  return c10::Dispatcher::singleton().findSchemaOrThrow(name, "");
+}
+
+// The rewrite runs at the autograd key: it reads and edits the graph behind loss.grad_fn and
+// returns the loss itself, so nothing below autograd is involved for real tensors.
+at::Tensor backward_filter_ad(at::Tensor loss, at::Tensor mask) {
+  if (traced(loss) || traced(mask)) {
+    at::AutoDispatchBelowADInplaceOrView guard;
+    static auto op = op_handle("token_filter::backward_filter")
+                         .typed<at::Tensor(at::Tensor, at::Tensor)>();
+    return op.call(loss, mask);
+  }
+  return backward_filter(loss, mask);
+}
+
+std::string backward_filter_with_dims_ad(at::Tensor loss, at::Tensor mask, std::string dims) {
+  if (traced(loss) || traced(mask)) {
+    at::AutoDispatchBelowADInplaceOrView guard;
+    static auto op = op_handle("token_filter::backward_filter_with_dims")
+                         .typed<std::string(at::Tensor, at::Tensor, std::string)>();
+    return op.call(loss, mask, dims);
+  }
+  return backward_filter_with_dims(loss, mask, dims);
+}
+
+std::vector<std::string> collect_node_names_ad(at::Tensor loss) {
+  if (traced(loss)) {
+    at::AutoDispatchBelowADInplaceOrView guard;
+    static auto op = op_handle("token_filter::collect_node_names")
+                         .typed<std::vector<std::string>(at::Tensor)>();
+    return op.call(loss);
+  }
+  return collect_node_names(loss);
+}
+
+}  // namespace
+}  // namespace cfb_filter
+
+TORCH_LIBRARY_IMPL(token_filter, Autograd, m) {
+  m.impl("backward_filter", &cfb_filter::backward_filter_ad);
+  m.impl("backward_filter_with_dims", &cfb_filter::backward_filter_with_dims_ad);
+  m.impl("collect_node_names", &cfb_filter::collect_node_names_ad);
+}
+
+// Tensors without autograd keys (inference mode) reach the backend kernels directly.
+TORCH_LIBRARY_IMPL(token_filter, CPU, m) {
+  m.impl("backward_filter", &cfb_filter::backward_filter);
+  m.impl("backward_filter_with_dims", &cfb_filter::backward_filter_with_dims);
+  m.impl("collect_node_names", &cfb_filter::collect_node_names);
+}
+
+TORCH_LIBRARY_IMPL(token_filter, CUDA, m) {
   m.impl("backward_filter", &cfb_filter::backward_filter);
   m.impl("backward_filter_with_dims", &cfb_filter::backward_filter_with_dims);
   m.impl("collect_node_names", &cfb_filter::collect_node_names);

@@ -186,6 +186,20 @@ Tensor Shrinker::gather_seq(const Tensor& t, int dim, int bdim, bool minus1) {
     shape[0] = B_;
     return gather_seq(t.expand(shape), dim, 0, minus1);
   }
+  if (B_ > 1 && bdim < 0 && dim != 0 && t.dim() >= 2 && t.size(0) > B_ &&
+      t.size(0) % B_ == 0) {
+    // batch folded into dim 0, batch-major (the [B*heads, S, *] operands of a batched matmul
+    // over [B, heads, S, *]): unfold it so that every sequence keeps its own positions (the
+    // reference uses sequence 0's positions here, graph_filter.cpp:216-221), then fold back
+    std::vector<int64_t> shape = t.sizes().vec();
+    shape[0] = t.size(0) / B_;
+    shape.insert(shape.begin(), B_);
+    const Tensor r = gather_seq(t.reshape(shape), dim + 1, 0, minus1);
+    std::vector<int64_t> out = r.sizes().vec();
+    out[1] *= out[0];
+    out.erase(out.begin());
+    return r.reshape(out);
+  }
   if (B_ == 1 || bdim < 0) {
     // no batch dimension: every row must share the kept positions; use row 0
     return t.index_select(dim, pos.select(0, 0).to(t.device()));

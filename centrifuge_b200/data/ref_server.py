@@ -75,6 +75,28 @@ def obtain_ref_loss(model, messages: Sequence[Sequence[int]], pad_id: int = 0,
     return pickle.dumps({"loss": res}) if return_pickle else res
 
 
+@torch.inference_mode()
+def obtain_ref_loss_cross_tokenizer(model, tokenizer, target_input_ids: Sequence[Sequence[int]],
+                                    target_tokenizer, device=None, tokenize_args=None,
+                                    return_pickle: bool = False):
+    """Reference losses for target-tokenized messages when the reference model has its own
+    tokenizer (model/utils.py:76-106 with ``manuel_matching``): decode the target ids, tokenize
+    the text with the reference tokenizer, compute the reference model's per-token losses and
+    move them onto the target tokens (:func:`centrifuge_b200.data.align.align_ref_target_tokens`).
+    Returns ``len(m) - 1`` losses per target message."""
+    from .align import align_ref_target_tokens, tokenized_prompts
+    strip_bos = bool(getattr(target_tokenizer, "add_bos_token", False))
+    texts = target_tokenizer.batch_decode([list(m)[1:] if strip_bos else list(m)
+                                           for m in target_input_ids])
+    ref_ids = [list(x) for x in tokenizer(texts, **(tokenize_args or {}))["input_ids"]]
+    pad = getattr(tokenizer, "pad_token_id", None)
+    losses = obtain_ref_loss(model, ref_ids, pad_id=0 if pad is None else pad, device=device)
+    aligned = align_ref_target_tokens(tokenized_prompts(tokenizer, ref_ids),
+                                      tokenized_prompts(target_tokenizer, target_input_ids),
+                                      losses)
+    return pickle.dumps({"loss": aligned}) if return_pickle else aligned
+
+
 class NGramModel:
     """Bigram / trigram reference loss from count tables.
 

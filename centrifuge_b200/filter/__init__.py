@@ -33,12 +33,33 @@ __all__ = ["backward_filter", "backward_filter_with_dims", "collect_node_names",
 _C = None
 
 
+def _register_fakes() -> None:
+    """FakeTensor (meta) kernels of the three operators, so that ``torch.compile`` and other
+    fake-tensor tracers can trace graphs that call them (reference ops.py:45-55): the rewrite
+    itself happens at run time; under tracing the loss passes through unchanged in shape."""
+
+    @torch.library.register_fake("token_filter::backward_filter")
+    def _fake_backward_filter(loss: Tensor, mask: Tensor) -> Tensor:
+        return torch.empty_like(loss)
+
+    @torch.library.register_fake("token_filter::backward_filter_with_dims")
+    def _fake_backward_filter_with_dims(loss: Tensor, mask: Tensor, dims: str) -> str:
+        return ""
+
+    @torch.library.register_fake("token_filter::collect_node_names")
+    def _fake_collect_node_names(loss: Tensor) -> List[str]:
+        return []
+
+
 def load():
-    """Import the rewriter extension (registers ``torch.ops.token_filter``) and the kernels
-    (registers ``torch.ops.cfb`` used by the filtered attention node on CUDA)."""
+    """Import the rewriter extension (registers ``torch.ops.token_filter`` and their fake
+    kernels) and the kernels (registers ``torch.ops.cfb`` used by the filtered attention node
+    on CUDA)."""
     global _C
     if _C is None:
-        _C = importlib.import_module("centrifuge_b200._filter_C")
+        mod = importlib.import_module("centrifuge_b200._filter_C")
+        _register_fakes()
+        _C = mod
         try:
             importlib.import_module("centrifuge_b200._kernels")
         except ImportError:
