@@ -1,4 +1,5 @@
-"""Kernel microbenchmarks: tcgen05 GEMM vs cuBLAS, attention fwd / filtered bwd.
+"""Kernel microbenchmarks: tcgen05 GEMM vs cuBLAS, attention fwd / filtered bwd vs the
+reference's ATen attention path (flash + memory-efficient backward) and cuDNN.
 
     python -m centrifuge_b200.benchmarks.kernel_bench [--json out.json]
 
@@ -111,7 +112,122 @@ def bench_fusions(T=16384, Tk=8192, H=2048, F=5632):
     return res
 
 
-def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3)):
+def _heads_major(x, B, S, n, hd):
+    """[B*S, n*hd] token-major rows -> [B, n, S, hd] (a view)."""
+    return x.view(B, S, n, hd).transpose(1, 2)
+
+
+def _repeat_kv(x, rep):
+    """[B, nkv, S, hd] -> [B, nkv*rep, S, hd] (K/V repeated per query head, as the reference's
+    pinned transformers does before SDPA)."""
+    B, n, S, hd = x.shape
+    return x[:, :, None].expand(B, n, rep, S, hd).reshape(B, n * rep, S, hd)
+
+
+def bench_attention_reference(qkv, B, S, nh, nkv, hd, pos_by_keep, res):
+    """The reference's attention on ATen kernels, same shapes.
+
+    Forward: dense causal flash attention over K/V repeated to the query heads (HF SDPA path of
+    transformers 4.45.2).  Filtered backward (grad_filter/token_filter/csrc/backward_filters.cpp:
+    420-486, RESTORE_Q): flash attention backward over kept queries x kept keys (is_causal), plus
+    the memory-efficient attention backward over kept queries x dropped keys with a
+    [B, heads, S_keep, S_drop] additive causal bias, whose dQ is added to the first; dK/dV of
+    the dropped keys are computed there and discarded, as in the reference.  The bias is built
+    once outside the timed region (the reference builds it once per graph).  Also timed: the
+    dense flash backward and cuDNN attention forward + backward (unfiltered baselines).
+    """
+    aten = torch.ops.aten
+    scale = 1.0 / math.sqrt(hd)
+    rep = nh // nkv
+    q = _heads_major(qkv[:, :nh * hd], B, S, nh, hd)
+    k = _repeat_kv(_heads_major(qkv[:, nh * hd:(nh + nkv) * hd], B, S, nkv, hd), rep)
+    v = _repeat_kv(_heads_major(qkv[:, (nh + nkv) * hd:], B, S, nkv, hd), rep)
+    fwd = aten._scaled_dot_product_flash_attention(q, k, v, 0.0, True, False, scale=scale)
+    out, lse, cq, ck, mq, mk, seed, off = fwd[:8]
+    fl_f = 4.0 * B * nh * hd * S * S / 2
+    ms = _time(lambda: aten._scaled_dot_product_flash_attention(q, k, v, 0.0, True, False,
+                                                                scale=scale), iters=10)
+    res.append({"name": "aten_flash_fwd_dense", "ms": ms, "tflops": fl_f / ms / 1e9})
+    print(json.dumps(res[-1]))
+    dout = torch.randn_like(out)
+    ms = _time(lambda: aten._scaled_dot_product_flash_attention_backward(
+        dout, q, k, v, out, lse, cq, ck, mq, mk, 0.0, True, seed, off, scale=scale), iters=10)
+    res.append({"name": "aten_flash_bwd_dense", "ms": ms, "tflops": 2.5 * fl_f / ms / 1e9})
+    print(json.dumps(res[-1]))
+    try:
+        qc = q.detach().clone().requires_grad_()
+        kc = _heads_major(qkv[:, nh * hd:(nh + nkv) * hd], B, S, nkv, hd).detach().clone()
+        vc = _heads_major(qkv[:, (nh + nkv) * hd:], B, S, nkv, hd).detach().clone()
+        kc.requires_grad_()
+        vc.requires_grad_()
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            o_c = torch.nn.functional.scaled_dot_product_attention(qc, kc, vc, is_causal=True,
+                                                                   enable_gqa=True)
+            ms_f = _time(lambda: torch.nn.functional.scaled_dot_product_attention(
+                qc, kc, vc, is_causal=True, enable_gqa=True), iters=10)
+            g_c = torch.randn_like(o_c)
+
+            def fb():
+                o2 = torch.nn.functional.scaled_dot_product_attention(qc, kc, vc, is_causal=True,
+                                                                      enable_gqa=True)
+                torch.autograd.grad(o2, (qc, kc, vc), g_c)
+
+            ms_fb = _time(fb, iters=10)
+        res.append({"name": "cudnn_fwd_dense", "ms": ms_f, "tflops": fl_f / ms_f / 1e9})
+        print(json.dumps(res[-1]))
+        res.append({"name": "cudnn_bwd_dense", "ms": ms_fb - ms_f,
+                    "tflops": 2.5 * fl_f / (ms_fb - ms_f) / 1e9})
+        print(json.dumps(res[-1]))
+    except Exception as e:  # cuDNN attention unavailable for this shape
+        res.append({"name": "cudnn_dense", "error": str(e)[:200]})
+        print(json.dumps(res[-1]))
+    for keep, pos in pos_by_keep:
+        Sk = pos.shape[1]
+        Sd = S - Sk
+        keepm = torch.zeros(B, S, dtype=torch.bool, device="cuda")
+        keepm.scatter_(1, pos.long(), True)
+        drop = torch.stack([torch.nonzero(~keepm[b]).squeeze(1) for b in range(B)])
+
+        def rows(t, idx):  # [B, h, S, hd] -> [B, h, len(idx), hd] per batch row
+            return torch.stack([t[b].index_select(1, idx[b]) for b in range(B)]).contiguous()
+
+        q_k, k_k, v_k = rows(q, pos.long()), rows(k, pos.long()), rows(v, pos.long())
+        o_k = rows(out, pos.long())
+        lse_k = torch.stack([lse[b].index_select(1, pos[b].long()) for b in range(B)]).contiguous()
+        do_k = torch.randn_like(o_k)
+        fl = 4.0 * B * nh * hd * (Sk * Sk / 2) + 6.0 * B * nh * hd * (Sk * S / 2)
+        if Sd > 0:
+            k_d, v_d = rows(k, drop), rows(v, drop)
+            causal = torch.full((S, S), float("-inf"), device="cuda").triu_(1)
+            bias = torch.stack([causal.index_select(0, pos[b].long()).index_select(1, drop[b])
+                                for b in range(B)]).to(q.dtype)
+            bias = bias[:, None].expand(B, nh, Sk, Sd).contiguous()
+            zero = torch.zeros(1, dtype=torch.long, device="cuda")
+
+        def ref_bwd():
+            dq, dk, dv = aten._scaled_dot_product_flash_attention_backward(
+                do_k, q_k, k_k, v_k, o_k, lse_k, cq, ck, Sk, Sk, 0.0, True, seed, off,
+                scale=scale)
+            if Sd > 0:
+                r = aten._scaled_dot_product_efficient_attention_backward(
+                    do_k, q_k, k_d, v_d, bias, o_k, lse_k, zero, zero, 0.0,
+                    [True, True, True, False], False, scale=scale)
+                dq.add_(r[0])
+            return dq
+
+        try:
+            ms = _time(ref_bwd, iters=10)
+            res.append({"name": f"reference_aten_bwd_keep{keep}", "Sk": Sk, "ms": ms,
+                        "tflops": fl / ms / 1e9})
+        except Exception as e:
+            res.append({"name": f"reference_aten_bwd_keep{keep}", "Sk": Sk,
+                        "error": str(e)[:300]})
+        print(json.dumps(res[-1]))
+
+
+def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3),
+                    reference=True):
     ld = (nh + 2 * nkv) * hd
     qkv = torch.randn(B * S, ld, device="cuda").bfloat16()
     o, lse = fused.attn_fwd(qkv, B, S, nh, nkv, hd)
@@ -132,10 +248,12 @@ def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3
                     "tflops": fl_f / 2 / ms64 / 1e9})
         print(json.dumps(res[-1]))
     g = torch.Generator(device="cuda").manual_seed(0)
+    pos_by_keep = []
     for keep in keeps:
         Sk = int(S * keep) // 8 * 8
         pos = torch.stack([torch.randperm(S, device="cuda", generator=g)[:Sk].sort().values
                            for _ in range(B)]).int()
+        pos_by_keep.append((keep, pos))
         flat = (pos + torch.arange(B, device="cuda", dtype=torch.int32).view(B, 1) * S).reshape(-1)
         qkv_k = qkv[flat.long()].contiguous()
         o_k = o[flat.long()].contiguous()
@@ -156,6 +274,8 @@ def bench_attention(B=4, S=4096, nh=32, nkv=8, hd=128, keeps=(1.0, 0.7, 0.5, 0.3
             res.append({"name": f"attn_bwd_mma_sync_keep{keep}", "Sk": Sk, "ms": ms_m,
                         "tflops": fl / ms_m / 1e9})
             print(json.dumps(res[-1]))
+    if reference:
+        bench_attention_reference(qkv, B, S, nh, nkv, hd, pos_by_keep, res)
     return res
 
 
@@ -175,6 +295,8 @@ def main():
                     help="also time every fixed tile shape (bn 128, 256, 512 = CTA pair)")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--no-reference", action="store_true",
+                    help="skip the reference's ATen attention path (flash + efficient bwd)")
     ap.add_argument("--keeps", default="1.0,0.7,0.5,0.3",
                     help="kept fractions of the filtered attention backward benchmark")
     args = ap.parse_args()
@@ -204,7 +326,8 @@ def main():
     if not args.skip_attn:
         B, S, nh, nkv, hd = (int(x) for x in args.attn_shape.split(","))
         keeps = tuple(float(x) for x in args.keeps.split(","))
-        out["attention"] = bench_attention(B, S, nh, nkv, hd, keeps=keeps)
+        out["attention"] = bench_attention(B, S, nh, nkv, hd, keeps=keeps,
+                                           reference=not args.no_reference)
     if args.json:
         with open(args.json, "w") as f:
             json.dump(out, f, indent=1)
