@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--reducer", default="auto", choices=["auto", "nccl", "symm"])
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (quick checks only; not a benchmark config)")
+    ap.add_argument("--no-status", action="store_true",
+                    help="do not read the device status word each step (A/B of its cost)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--json-out", default=None)
     return ap.parse_args()
@@ -145,7 +147,8 @@ def main():
                     eps=1e-8, weight_decay=0.0, grad_clip=1.0, reducer=reducer)
     drop = 0.0 if args.mode == "regular" else args.drop
     trainer = Trainer(model, opt, drop_rate=drop, grad_accum=args.ga, world_size=world,
-                      filter_backward=args.mode == "centrifuge")
+                      filter_backward=args.mode == "centrifuge",
+                      check_device_errors=not args.no_status)
     data = SyntheticTokenData(cfg.vocab_size, args.mbs, args.seq, seed=4321, rank=rank)
 
     def barrier():
@@ -160,6 +163,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     counter.reset()
+    torch.cuda.reset_peak_memory_stats(dev)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record()
@@ -170,6 +174,7 @@ def main():
     barrier()
     torch.cuda.synchronize()
     launches = counter.reset()
+    peak_gb = torch.cuda.max_memory_allocated(dev) / 2 ** 30
     ms = start.elapsed_time(stop)
     t = torch.tensor([ms], device=dev)
     if world > 1:
@@ -216,6 +221,7 @@ def main():
                                    if opt.reducer else "none"),
                        "l2": "working set (weights + activations) far larger than L2"},
             "clocks": clocks.summary(), "gpu_launches": launches, "e2e": e2e,
+            "peak_mem_gib": round(peak_gb, 2),
             "loss": float(loss.item()),
         }
         print(json.dumps(line), flush=True)

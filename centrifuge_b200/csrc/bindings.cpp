@@ -153,6 +153,71 @@ void gemm_swiglu(const Tensor& x, const Tensor& w, Tensor& gu, Tensor& h) {
                "gemm_swiglu");
 }
 
+// lm_head forward fused with cross-entropy statistics: per row and 256-column tile of
+// x @ w^T the max and sum of exp (pmax, psum [M, ceil(N / 256)]) and the label logit (ptgt [M]);
+// the logits are never stored
+void gemm_ce_part(const Tensor& x, const Tensor& w, const Tensor& labels, Tensor& pmax,
+                  Tensor& psum, Tensor& ptgt) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0), nt = (N + 255) / 256;
+  TORCH_CHECK(w.size(1) == K, "gemm_ce_part: w must be [N, K]");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == M,
+              "gemm_ce_part: labels int64 [M]");
+  for (const Tensor* t : {&pmax, &psum})
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == M * nt,
+                "gemm_ce_part: pmax / psum fp32 [M, ceil(N / 256)]");
+  TORCH_CHECK(ptgt.scalar_type() == at::kFloat && ptgt.numel() == M, "gemm_ce_part: ptgt");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_gemm_ce_part(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                                static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                                pmax.data_ptr<float>(), psum.data_ptr<float>(),
+                                ptgt.data_ptr<float>(), err_word(x.get_device()).data_ptr<int>(),
+                                cur_stream()),
+               "gemm_ce_part");
+}
+
+// dlogits [M, N] = (softmax(x @ w^T) - onehot(labels)) * dloss with the logits recomputed
+void gemm_ce_grad(const Tensor& x, const Tensor& w, const Tensor& labels, const Tensor& lse,
+                  const Tensor& dloss, Tensor& out) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(out, "out");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && out.size(0) == M && out.size(1) == N, "gemm_ce_grad: shapes");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous() && labels.numel() == M,
+              "gemm_ce_grad: labels int64 [M]");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == M &&
+                  dloss.scalar_type() == at::kFloat && dloss.is_contiguous() &&
+                  dloss.numel() == M,
+              "gemm_ce_grad: lse / dloss fp32 [M]");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_gemm_ce_grad(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0),
+                                out.data_ptr(), out.stride(0), static_cast<int>(M),
+                                static_cast<int>(N), static_cast<int>(K),
+                                reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                                lse.data_ptr<float>(), dloss.data_ptr<float>(),
+                                err_word(x.get_device()).data_ptr<int>(), cur_stream()),
+               "gemm_ce_grad");
+}
+
+void ce_combine(const Tensor& pmax, const Tensor& psum, const Tensor& ptgt, const Tensor& labels,
+                Tensor& loss, Tensor& lse) {
+  const int64_t M = labels.numel();
+  TORCH_CHECK(M > 0 && pmax.numel() % M == 0 && psum.numel() == pmax.numel(),
+              "ce_combine: statistics");
+  const c10::cuda::CUDAGuard guard(pmax.device());
+  CFB_CHECK_RC(cfb_ce_combine(pmax.data_ptr<float>(), psum.data_ptr<float>(),
+                              ptgt.data_ptr<float>(), static_cast<int>(M),
+                              static_cast<int>(pmax.numel() / M),
+                              reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                              loss.data_ptr<float>(), lse.data_ptr<float>(), cur_stream()),
+               "ce_combine");
+}
+
 // (bn, ksplit, pair) the GEMM planner picks for an M x N x K problem on `sms` SMs (host only)
 std::tuple<int64_t, int64_t, bool> gemm_plan(int64_t M, int64_t N, int64_t K, int64_t epi,
                                              int64_t bn, int64_t sms) {
@@ -715,6 +780,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("peer_us"));
   m.def("zero_unless_error", &zero_unless_error);
   m.def("gemm_swiglu", &gemm_swiglu, "gate/up projection with the SwiGLU epilogue");
+  m.def("gemm_ce_part", &gemm_ce_part, "lm_head GEMM with cross-entropy statistics epilogue");
+  m.def("gemm_ce_grad", &gemm_ce_grad, "lm_head recompute GEMM with the cross-entropy gradient");
+  m.def("ce_combine", &ce_combine);
   m.def("gemm_plan", &gemm_plan, "tile / split-K choice of the GEMM planner (host only)");
   m.def("gemm_swiglu_bwd", &gemm_swiglu_bwd,
         "down-projection dgrad with the SwiGLU backward in the epilogue");

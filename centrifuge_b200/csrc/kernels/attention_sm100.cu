@@ -134,6 +134,7 @@ __device__ __forceinline__ bool group_exchange(float* vals, volatile int* flags,
   __threadfence_block();
   flags[grp * BMr + r] = seq;
   const uint64_t t0 = globaltimer_ns();
+  uint64_t limit = 0;  // read from the status block only once a wait has spun 256 times
 #pragma unroll
   for (int q = 0; q < NQ; ++q) {
     if (q == grp) continue;
@@ -141,7 +142,8 @@ __device__ __forceinline__ bool group_exchange(float* vals, volatile int* flags,
     while (flags[q * BMr + r] < seq) {
       if ((++spins & 255u) == 0) {
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > local_wait_limit_ns(err)) {
+        if (limit == 0) limit = local_wait_limit_ns(err);
+        if (globaltimer_ns() - t0 > limit) {
           *abort_flag = 1;
           atomicCAS(err, 0, kErrWaitSoftmax);
           return false;

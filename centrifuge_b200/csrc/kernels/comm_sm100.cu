@@ -46,14 +46,17 @@ __device__ __forceinline__ float4 multimem_ld_reduce_add_v4(const float* mc) {
 __device__ bool wait_flags(const uint32_t* flags, int base, int stride, int n, uint32_t epoch,
                            int* err, int code) {
   const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = peer_wait_limit_ns(err);
+  uint64_t limit = 0;  // read from the status block only once a wait has spun 1024 times
   for (int i = 0; i < n; ++i) {
     const uint32_t* f = flags + base + i * stride;
     uint32_t spins = 0;
     while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
-      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > limit) {
-        atomicCAS(err, 0, code);
-        return false;
+      if ((++spins & 1023u) == 0) {
+        if (limit == 0) limit = peer_wait_limit_ns(err);
+        if (globaltimer_ns() - t0 > limit) {
+          atomicCAS(err, 0, code);
+          return false;
+        }
       }
     }
   }

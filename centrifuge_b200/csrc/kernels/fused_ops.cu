@@ -834,6 +834,38 @@ int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float*
   return last_err();
 }
 
+// One warp per row: lse and loss from the per-tile statistics of the fused lm_head GEMM.
+__global__ void __launch_bounds__(256) ce_combine_kernel(
+    const float* __restrict__ pmax, const float* __restrict__ psum,
+    const float* __restrict__ ptgt, int rows, int nt, const long long* __restrict__ labels,
+    float* __restrict__ loss, float* __restrict__ lse) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* pm = pmax + static_cast<long long>(row) * nt;
+  const float* ps = psum + static_cast<long long>(row) * nt;
+  float m = -CUDART_INF_F;
+  for (int t = lane; t < nt; t += 32) m = fmaxf(m, pm[t]);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int t = lane; t < nt; t += 32) s += ps[t] * __expf(pm[t] - m);
+  s = warp_sum(s);
+  if (lane == 0) {
+    const float l = m + __logf(s);
+    lse[row] = l;
+    const long long lab = labels[row];
+    loss[row] = lab >= 0 ? l - ptgt[row] : 0.f;
+  }
+}
+
+int cfb_ce_combine(const float* pmax, const float* psum, const float* ptgt, int rows, int nt,
+                   const long long* labels, float* loss, float* lse, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  ce_combine_kernel<<<(rows + 7) / 8, 256, 0, st>>>(pmax, psum, ptgt, rows, nt, labels, loss,
+                                                    lse);
+  return last_err();
+}
+
 int cfb_ce_bwd(const void* logits, long long ld, const int* logit_rows, const long long* labels,
                const float* lse, const float* dloss, void* dlogits, long long ld_out, int rows,
                int V, long long vocab_start, cudaStream_t st) {

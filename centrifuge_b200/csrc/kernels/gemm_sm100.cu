@@ -26,6 +26,13 @@
 
 namespace cfb {
 
+// Hardware base-2 exponential (MUFU, ftz).
+__device__ __forceinline__ float exp2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct GemmArgs {
   int M, N, K;
   // split-K (kEpiF32Acc only): every output tile is computed as ksplit work units over
@@ -54,6 +61,13 @@ struct GemmArgs {
   // kEpiSwiGLUBwd: aux = gu [*, 2F] (read; gate at column n, up at dual_off + n) of row
   // aux_rows[m] (or m); D [M, 2F] receives d gate at column n and d up at dual_off + n
   const int* aux_rows;
+  // kEpiCEPart / kEpiCEGrad (256-column tiles): labels [M] (< 0: ignored row); per row and
+  // tile the statistics ce_pmax / ce_psum [M, ce_nt] and the label logit ce_ptgt [M]
+  // (forward); lse [M] and dloss [M] (backward, D = dlogits bf16)
+  const long long* ce_labels;
+  float *ce_pmax, *ce_psum, *ce_ptgt;
+  const float *ce_lse, *ce_dloss;
+  int ce_nt;
   // ---- tensor-parallel fusion.  Row segments: rank q owns rows [seg[q], seg[q+1]) of A / D
   // (device array [P + 1]; uniform shards in the forward, kept rows in the backward).  Flags
   // live in symmetric buffers peer_flags[q]: ready[P] at flag_ready, done[P] at flag_done.
@@ -109,12 +123,13 @@ __device__ __forceinline__ void st_release_sys(uint32_t* f, uint32_t v) {
 __device__ __forceinline__ bool wait_epoch(const uint32_t* flags, int n, uint32_t epoch,
                                            volatile int* abort, int* err) {
   const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = peer_wait_limit_ns(err);
+  uint64_t limit = 0;  // read from the status block only once a wait has spun 256 times
   for (int i = 0; i < n; ++i) {
     uint32_t spins = 0;
     while (static_cast<int32_t>(ld_acquire_sys(flags + i) - epoch) < 0) {
       if ((++spins & 255u) == 0) {
         if (*abort) return false;
+        if (limit == 0) limit = peer_wait_limit_ns(err);
         if (globaltimer_ns() - t0 > limit) {
           *abort = 1;
           atomicCAS(err, 0, kErrPeerWait);
@@ -171,6 +186,72 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& p, uint32_t taddr, 
   constexpr bool DUAL = EPI == kEpiSwiGLU;
   const int ksplit = p.ksplit;
   (void)ksplit;
+  if (EPI == kEpiCEPart) {
+    // online max / sum of exp over the tile's columns, in log2 units; fp32 logits
+    constexpr float kL2e = 1.4426950408889634f, kLn2f = 0.6931471805599453f;
+    const long long lab = row < p.M ? p.ce_labels[row] : -1;
+    float m = -INFINITY, sum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = n0 + c * 32;
+      if (col >= p.N) break;  // warp-uniform (N % 32 == 0)
+      uint32_t r[32];
+      CFB_TMEM_LD32(taddr + c * 32, r);
+      tmem_ld_wait();
+      float cm = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) cm = fmaxf(cm, __uint_as_float(r[i]));
+      const float mn = fmaxf(m, cm * p.alpha * kL2e);
+      float acc = (m == -INFINITY) ? 0.f : sum * exp2f_approx(m - mn);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc += exp2f_approx(fmaf(__uint_as_float(r[i]), p.alpha * kL2e, -mn));
+      sum = acc;
+      m = mn;
+      if (lab >= col && lab < col + 32) {
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (lab - col == i) t = __uint_as_float(r[i]);
+        p.ce_ptgt[row] = t * p.alpha;
+      }
+    }
+    if (row < p.M) {
+      const long long o = static_cast<long long>(row) * p.ce_nt + n0 / BN;
+      p.ce_pmax[o] = m * kLn2f;
+      p.ce_psum[o] = sum;
+    }
+    return;
+  }
+  if (EPI == kEpiCEGrad) {
+    constexpr float kL2e = 1.4426950408889634f;
+    const bool live = row < p.M;
+    const long long lab = live ? p.ce_labels[row] : -1;
+    const float nl = live ? -p.ce_lse[row] * kL2e : 0.f;
+    const float dl = (live && lab >= 0) ? p.ce_dloss[row] : 0.f;
+    __nv_bfloat16* grow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int col = n0 + c * 32;
+      if (col >= p.N) break;  // warp-uniform
+      uint32_t r[32];
+      CFB_TMEM_LD32(taddr + c * 32, r);
+      tmem_ld_wait();
+      if (!live) continue;
+      uint32_t o[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        float g0 = exp2f_approx(fmaf(__uint_as_float(r[2 * t]), p.alpha * kL2e, nl));
+        float g1 = exp2f_approx(fmaf(__uint_as_float(r[2 * t + 1]), p.alpha * kL2e, nl));
+        if (lab == col + 2 * t) g0 -= 1.f;
+        if (lab == col + 2 * t + 1) g1 -= 1.f;
+        o[t] = pack_bf16x2(g0 * dl, g1 * dl);
+      }
+      uint4* d4 = reinterpret_cast<uint4*>(grow + col);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) d4[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+    }
+    return;
+  }
   __nv_bfloat16* drow = reinterpret_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
 #pragma unroll 1
   for (int c = 0; c < BN / 32; ++c) {
@@ -1098,6 +1179,12 @@ static int dispatch_pair(int epi, bool a_mn, bool b_mn, const CUtensorMap& ta,
     case kEpiSwiGLUBwd:  // down-projection dgrad only: A K-major, B MN-major
       if (a_mn || !b_mn) return -4;
       return launch_gemm_pair<false, true, kEpiSwiGLUBwd>(ta, tb, a, st);
+    case kEpiCEPart:  // lm_head forward / recompute: both operands K-major
+      if (a_mn || b_mn) return -4;
+      return launch_gemm_pair<false, false, kEpiCEPart>(ta, tb, a, st);
+    case kEpiCEGrad:
+      if (a_mn || b_mn) return -4;
+      return launch_gemm_pair<false, false, kEpiCEGrad>(ta, tb, a, st);
   }
   return -4;
 }
@@ -1160,6 +1247,11 @@ struct EpiExtra {
   const void* aux;
   long long ld_aux;
   const int* aux_rows;
+  // cross-entropy epilogues
+  const long long* ce_labels = nullptr;
+  float *ce_pmax = nullptr, *ce_psum = nullptr, *ce_ptgt = nullptr;
+  const float *ce_lse = nullptr, *ce_dloss = nullptr;
+  int ce_nt = 0;
 };
 
 static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, long long ldb,
@@ -1231,6 +1323,13 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   a.aux = ex ? const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(ex->aux)) : nullptr;
   a.ld_aux = ex ? ex->ld_aux : 0;
   a.aux_rows = ex ? ex->aux_rows : nullptr;
+  a.ce_labels = ex ? ex->ce_labels : nullptr;
+  a.ce_pmax = ex ? ex->ce_pmax : nullptr;
+  a.ce_psum = ex ? ex->ce_psum : nullptr;
+  a.ce_ptgt = ex ? ex->ce_ptgt : nullptr;
+  a.ce_lse = ex ? ex->ce_lse : nullptr;
+  a.ce_dloss = ex ? ex->ce_dloss : nullptr;
+  a.ce_nt = ex ? ex->ce_nt : 0;
   a.rank = 0;
   a.P = 1;
   a.seg = nullptr;
@@ -1300,10 +1399,38 @@ static int gemm_entry(const void* A, long long lda, int a_mn, const void* B, lon
   return dispatch_epi<128>(epi, a_mn, b_mn, ta, tb, a, st, max_ctas);
 }
 
+int cfb_gemm_ce_part(const void* X, long long ldx, const void* W, long long ldw, int M, int N,
+                     int K, const long long* labels, float* pmax, float* psum, float* ptgt,
+                     int* err, cudaStream_t st) {
+  if (!labels || !pmax || !psum || !ptgt) return -13;
+  EpiExtra ex{0, nullptr, 0, nullptr};
+  ex.ce_labels = labels;
+  ex.ce_pmax = pmax;
+  ex.ce_psum = psum;
+  ex.ce_ptgt = ptgt;
+  ex.ce_nt = (N + 255) / 256;
+  return gemm_entry(X, ldx, 0, W, ldw, 0, nullptr, 0, kEpiCEPart, nullptr, 0, M, N, K, 1.0f,
+                    err, kGemmTilePair, 0, nullptr, nullptr, 0, 0, nullptr, st, &ex);
+}
+
+int cfb_gemm_ce_grad(const void* X, long long ldx, const void* W, long long ldw, void* dlogits,
+                     long long ldd, int M, int N, int K, const long long* labels,
+                     const float* lse, const float* dloss, int* err, cudaStream_t st) {
+  if (!labels || !lse || !dloss || !dlogits || (ldd % 8)) return -13;
+  EpiExtra ex{0, nullptr, 0, nullptr};
+  ex.ce_labels = labels;
+  ex.ce_lse = lse;
+  ex.ce_dloss = dloss;
+  return gemm_entry(X, ldx, 0, W, ldw, 0, dlogits, ldd, kEpiCEGrad, nullptr, 0, M, N, K, 1.0f,
+                    err, kGemmTilePair, 0, nullptr, nullptr, 0, 0, nullptr, st, &ex);
+}
+
 int cfb_gemm_bf16(const void* A, long long lda, int a_mn, const void* B, long long ldb, int b_mn,
                   void* D, long long ldd, int epi, const void* R, long long ldr, int M, int N,
                   int K, float alpha, int* err, int bn, int max_ctas, cudaStream_t st) {
-  if (epi == kEpiBF16Rope || epi == kEpiSwiGLU || epi == kEpiSwiGLUBwd) return -4;
+  if (epi == kEpiBF16Rope || epi == kEpiSwiGLU || epi == kEpiSwiGLUBwd || epi == kEpiCEPart ||
+      epi == kEpiCEGrad)
+    return -4;
   return gemm_entry(A, lda, a_mn, B, ldb, b_mn, D, ldd, epi, R, ldr, M, N, K, alpha, err, bn,
                     max_ctas, nullptr, nullptr, 0, 0, nullptr, st);
 }

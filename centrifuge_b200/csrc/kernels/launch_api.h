@@ -13,7 +13,9 @@ enum {
   kEpiF32Acc = 3,
   kEpiBF16Rope = 4,
   kEpiSwiGLU = 5,
-  kEpiSwiGLUBwd = 6  // dgrad of the down projection -> d[gate; up] (see cfb_gemm_swiglu_bwd)
+  kEpiSwiGLUBwd = 6,  // dgrad of the down projection -> d[gate; up] (see cfb_gemm_swiglu_bwd)
+  kEpiCEPart = 7,     // lm_head forward fused with cross-entropy statistics (cfb_gemm_ce_part)
+  kEpiCEGrad = 8      // lm_head recompute fused with the cross-entropy gradient (cfb_gemm_ce_grad)
 };
 // `bn` value of cfb_gemm_bf16 that selects the 256 x 256 tile on a CTA pair (cta_group::2);
 // 128 / 256 select a single-CTA tile of that width, 0 lets the planner choose
@@ -165,6 +167,26 @@ int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, c
                     long long ld_o, const float* lse_k, const float* delta, const int* pos_k,
                     void* dqkv_k, int B, int S, int Sk, int nh, int nkv, int hd, float scale,
                     const float* rope_cs, int* work, int* err, cudaStream_t st);
+
+// lm_head GEMM fused with cross entropy (gemm_sm100.cu, CTA-pair tiles of 256 x 256).
+// Forward: logits = X W^T (X [M, K], W [N, K], both K-major) are never stored; for every row r
+// and 256-column tile t the epilogue writes pmax[r * nt + t] = max of the tile's fp32 logits,
+// psum[r * nt + t] = sum of exp(logit - pmax) over them, and ptgt[r] = the logit of column
+// labels[r] (written by the tile that holds it; rows with labels[r] < 0 get nothing).
+// nt = ceil(N / 256).  cfb_ce_combine then gives lse and the per-token loss.
+int cfb_gemm_ce_part(const void* X, long long ldx, const void* W, long long ldw, int M, int N,
+                     int K, const long long* labels, float* pmax, float* psum, float* ptgt,
+                     int* err, cudaStream_t st);
+// Backward: logits of the M rows of X recomputed in the GEMM, the epilogue stores
+// dlogits[r, c] = (exp(logit - lse[r]) - [c == labels[r]]) * dloss[r] (bf16, ld ldd; zero rows
+// for labels[r] < 0).
+int cfb_gemm_ce_grad(const void* X, long long ldx, const void* W, long long ldw, void* dlogits,
+                     long long ldd, int M, int N, int K, const long long* labels,
+                     const float* lse, const float* dloss, int* err, cudaStream_t st);
+// lse[r] = M + log(sum_t psum[r, t] exp(pmax[r, t] - M)), M = max_t pmax[r, t];
+// loss[r] = lse[r] - ptgt[r] for labels[r] >= 0, else 0.
+int cfb_ce_combine(const float* pmax, const float* psum, const float* ptgt, int rows, int nt,
+                   const long long* labels, float* loss, float* lse, cudaStream_t st);
 
 // NVLink peer-memory gradient reduction (comm_sm100.cu).
 int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,

@@ -94,11 +94,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = local_wait_limit_ns(err);
+  uint64_t limit = 0;  // read from the status block only once a wait has spun 64 times
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
+      if (limit == 0) limit = local_wait_limit_ns(err);
       if (globaltimer_ns() - t0 > limit) {
         *abort = 1;
         if (err) atomicCAS(err, 0, code);

@@ -23,6 +23,8 @@ Weights are stored fused (``wqkv = [q; k; v]``, ``wgu = [gate; up]``) in one fla
 """
 from __future__ import annotations
 
+import os
+
 import math
 from dataclasses import dataclass
 from typing import Callable, Dict, List, Optional, Tuple
@@ -91,6 +93,9 @@ class LlamaCore(torch.nn.Module):
         self.layer_ids = range(self.first, self.last)
         self.has_embed, self.has_head = has_embed, has_head
         self.keep_logits = keep_logits
+        # CUDA: lm_head + cross entropy fused (no [T, V] logits kept between forward and
+        # backward; the kept rows' logits are recomputed).  CFB_FUSED_CE=0 keeps the logits.
+        self.fused_ce = os.environ.get("CFB_FUSED_CE", "1") != "0"
         self.flat = FlatParams(param_specs(cfg, self.layer_ids, has_embed, has_head), device,
                                dtype=dtype, pad_to=pad_to)
         self.device = self.flat.device
@@ -178,14 +183,20 @@ class LlamaCore(torch.nn.Module):
         if not self.has_head:
             return x, sv
         xf, rstdf = fused.rmsnorm_fwd(x, p["norm"], cfg.rms_norm_eps)
-        logits = G.linear_fwd(xf, p["lm_head"])
         if labels is None:
             lab = torch.full((B, S), -100, dtype=torch.long, device=x.device)
             lab[:, :-1] = input_ids[:, 1:]
         else:
             lab = labels.to(torch.long).clone()
         lab = lab.reshape(-1).contiguous()
-        loss, lse_ce = fused.ce_fwd(logits, lab)
+        if self.fused_ce and x.is_cuda and not self.keep_logits:
+            # lm_head GEMM with the cross-entropy statistics in its epilogue: the [T, V] logits
+            # are never stored; the backward recomputes them for the kept rows only
+            logits = None
+            loss, lse_ce = G.linear_fwd_ce(xf, p["lm_head"], lab)
+        else:
+            logits = G.linear_fwd(xf, p["lm_head"])
+            loss, lse_ce = fused.ce_fwd(logits, lab)
         sv.head = dict(x=x, xf=xf, rstdf=rstdf, logits=logits, labels=lab, lse=lse_ce)
         self._last_logits = logits if self.keep_logits else None
         token_loss = loss.view(B, S)[:, :-1].contiguous()
@@ -225,8 +236,15 @@ class LlamaCore(torch.nn.Module):
                 dl = torch.gather(dl, 1, idx)
             dl = torch.cat([dl, torch.zeros(B, 1, device=dl.device, dtype=dl.dtype)], 1)
             dloss = dl.reshape(-1).contiguous()
-            dlogits = fused.ce_bwd(hd_["logits"], hd_["labels"], hd_["lse"], dloss, rows)
             xf_k = self._gather(hd_["xf"], rows)
+            if hd_["logits"] is None:
+                # recompute the kept rows' logits inside the GEMM; its epilogue writes dlogits
+                lab_k, lse_k = hd_["labels"], hd_["lse"]
+                if rows is not None:
+                    lab_k, lse_k = lab_k[rows.long()], lse_k[rows.long()]
+                dlogits = G.linear_ce_grad(xf_k, p["lm_head"], lab_k, lse_k, dloss)
+            else:
+                dlogits = fused.ce_bwd(hd_["logits"], hd_["labels"], hd_["lse"], dloss, rows)
             G.linear_wgrad(dlogits, xf_k, g["lm_head"])
             dxf = G.linear_dgrad(dlogits, p["lm_head"])
             del dlogits, xf_k

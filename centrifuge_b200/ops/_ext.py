@@ -13,7 +13,8 @@ _err = None
 _proxy = None
 
 # Kernels launched by one call of each binding (for the launch counter).
-_LAUNCHES_PER_CALL = {"rmsnorm_bwd": 2, "attn_bwd": 2, "attn_bwd_mma": 3, "gemm_error_word": 0}
+_LAUNCHES_PER_CALL = {"rmsnorm_bwd": 2, "attn_bwd": 2, "attn_bwd_mma": 3, "gemm_error_word": 0,
+                      "status_block": 0, "set_wait_limits": 0, "gemm_plan": 0}
 
 
 class LaunchCounter:
@@ -70,3 +71,17 @@ def available() -> bool:
         return True
     except RuntimeError:
         return False
+
+
+def status_block(device=None):
+    """The kernels' per-device status block (error word + wait limits) of ``device`` (a
+    ``torch.device``, an index, or None for the current CUDA device)."""
+    import torch
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, int):
+        idx = device
+    else:
+        d = torch.device(device)
+        idx = d.index if d.index is not None else torch.cuda.current_device()
+    return kernels().status_block(idx)

@@ -62,6 +62,42 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, out: Optional[torch.Tensor] = N
                 resid)
 
 
+def linear_fwd_ce(x: torch.Tensor, w: torch.Tensor, labels: torch.Tensor):
+    """Per-token cross entropy of ``logits = x w^T`` against ``labels`` (< 0: ignored, loss 0)
+    without storing the logits: the GEMM epilogue reduces every 256-column tile of a row to
+    (max, sum of exp, label logit) and a combine kernel forms ``lse`` and the loss.
+    Returns ``(loss [M], lse [M])`` in fp32."""
+    M, N = x.shape[0], w.shape[0]
+    f32 = dict(dtype=torch.float32, device=x.device)
+    if not x.is_cuda:
+        from . import reference as ref
+        return ref.cross_entropy(x.float() @ w.float().t(), labels)
+    nt = (N + 255) // 256
+    pmax = torch.empty(M, nt, **f32)
+    psum = torch.empty(M, nt, **f32)
+    ptgt = torch.empty(M, **f32)
+    loss, lse = torch.empty(M, **f32), torch.empty(M, **f32)
+    k = kernels()
+    k.gemm_ce_part(x, w, labels, pmax, psum, ptgt)
+    k.ce_combine(pmax, psum, ptgt, labels, loss, lse)
+    return loss, lse
+
+
+def linear_ce_grad(x: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, lse: torch.Tensor,
+                   dloss: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``dlogits = (softmax(x w^T) - onehot(labels)) * dloss`` (bf16 ``[M, N]``) with the logits
+    recomputed inside the GEMM (rows with ``labels < 0`` are zero)."""
+    M, N = x.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    if not x.is_cuda:
+        from . import reference as ref
+        out.copy_(ref.cross_entropy_bwd(x.float() @ w.float().t(), labels, lse, dloss))
+        return out
+    kernels().gemm_ce_grad(x, w, labels, lse.contiguous(), dloss.contiguous(), out)
+    return out
+
+
 def linear_fwd_rope(x: torch.Tensor, w: torch.Tensor, pos: torch.Tensor, table: torch.Tensor,
                     rope_cols: int, head_dim: int, out: Optional[torch.Tensor] = None
                     ) -> torch.Tensor:

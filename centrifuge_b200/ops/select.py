@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from ._ext import kernels
+from ._ext import kernels, status_block
 
 
 def drop_smallest_(score: torch.Tensor, mask: torch.Tensor, k: int, start: int, end: int):
@@ -42,6 +42,6 @@ def keep_index(mask: torch.Tensor, s_keep: int):
     m = m.contiguous()
     pos = torch.empty(B, s_keep, dtype=torch.int32, device=mask.device)
     flat = torch.empty(B * s_keep, dtype=torch.int32, device=mask.device)
-    err = kernels().status_block(mask.device.index)
+    err = status_block(mask.device)
     kernels().keep_index(m, s_keep, pos, flat, err)
     return pos, flat, err

@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from ..ops._ext import kernels
+from ..ops._ext import kernels, status_block
 
 MAX_BUCKETS = 4096
 
@@ -56,7 +56,7 @@ class SymmReducer:
         self.fhdl = symm_mem.rendezvous(self.flags, group)
         self.peer_flags_dev = int(self.fhdl.buffer_ptrs_dev)
         # the kernels' per-device status block (error word + wait limits)
-        self.err = kernels().status_block(dev.index)
+        self.err = status_block(dev)
         self.epoch = 1
         self.base_ptr = buf.data_ptr()
         torch.cuda.synchronize(dev)

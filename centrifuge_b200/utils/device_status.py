@@ -52,8 +52,8 @@ class DeviceStatus:
     def __init__(self, device, block: Optional[torch.Tensor] = None):
         self.device = torch.device(device)
         if block is None:
-            from ..ops._ext import kernels
-            block = kernels().status_block(self.device.index or 0)
+            from ..ops._ext import status_block
+            block = status_block(self.device)
         self.block = block
         self.async_copy = block.is_cuda
         self.host = torch.zeros(2, block.numel(), dtype=torch.int32,
@@ -65,7 +65,8 @@ class DeviceStatus:
     def set_wait_limits(self, local_s: float = 0.0, peer_s: float = 0.0) -> None:
         """Limits of the bounded device waits (seconds; 0 = default)."""
         from ..ops._ext import kernels
-        kernels().set_wait_limits(self.device.index or 0, int(local_s * 1e6), int(peer_s * 1e6))
+        idx = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        kernels().set_wait_limits(idx, int(local_s * 1e6), int(peer_s * 1e6))
 
     def _check_row(self, slot: int) -> None:
         code = int(self.host[slot, 0])

@@ -399,3 +399,28 @@ def test_attention_bwd_filtered(B, S, nh, nkv, hd, keep):
     kernels().attn_bwd_mma(qkv_k, qkv, o_k, do_k, lse_k, pos.reshape(-1), d2, delta, B, S, Sk, nh,
                            nkv, hd, 1.0 / hd ** 0.5)
     assert rel_err(d2, d) < 2e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1056, 256), (512, 32000, 2048), (1, 320, 64)])
+def test_fused_lm_head_cross_entropy(M, N, K):
+    """lm_head GEMM with the cross-entropy statistics in its epilogue (logits never stored) and
+    the backward recompute with the dlogits epilogue, against fp32 cross entropy."""
+    torch.manual_seed(12)
+    x = (torch.randn(M, K, device=dev) * 0.5).bfloat16()
+    w = (torch.randn(N, K, device=dev) / K ** 0.5).bfloat16()
+    labels = torch.randint(0, N, (M,), device=dev)
+    labels[::7] = -100
+    loss, lse = gemm.linear_fwd_ce(x, w, labels)
+    logits = x.float() @ w.float().t()
+    loss_r, lse_r = ref.cross_entropy(logits, labels)
+    assert (lse - lse_r).abs().max().item() < 2e-3 * max(1.0, lse_r.abs().max().item())
+    assert (loss - loss_r).abs().max().item() < 2e-3 * max(1.0, loss_r.abs().max().item())
+    assert bool((loss[labels < 0] == 0).all())
+    dloss = torch.rand(M, device=dev)
+    g = gemm.linear_ce_grad(x, w, labels, lse, dloss)
+    g_r = ref.cross_entropy_bwd(logits, labels, lse_r, dloss)
+    err = ((g.float() - g_r).norm() / (g_r.norm() + 1e-12)).item()
+    assert err < 1e-2, err
+    assert float(g[labels < 0].float().abs().sum()) == 0.0
+    from centrifuge_b200.ops import kernels
+    assert kernels().gemm_error_word(0, True) == 0
