@@ -205,7 +205,7 @@ void gemm_ce_grad(const Tensor& x, const Tensor& w, const Tensor& labels, const 
 }
 
 void ce_combine(const Tensor& pmax, const Tensor& psum, const Tensor& ptgt, const Tensor& labels,
-                Tensor& loss, Tensor& lse) {
+                int64_t vocab, Tensor& loss, Tensor& lse) {
   const int64_t M = labels.numel();
   TORCH_CHECK(M > 0 && pmax.numel() % M == 0 && psum.numel() == pmax.numel(),
               "ce_combine: statistics");
@@ -214,7 +214,8 @@ void ce_combine(const Tensor& pmax, const Tensor& psum, const Tensor& ptgt, cons
                               ptgt.data_ptr<float>(), static_cast<int>(M),
                               static_cast<int>(pmax.numel() / M),
                               reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
-                              loss.data_ptr<float>(), lse.data_ptr<float>(), cur_stream()),
+                              vocab, loss.data_ptr<float>(), lse.data_ptr<float>(),
+                              err_word(pmax.get_device()).data_ptr<int>(), cur_stream()),
                "ce_combine");
 }
 
@@ -441,9 +442,10 @@ void gather_rows(const Tensor& src, const Tensor& idx, Tensor& dst) {
   const int64_t es = src.element_size();
   if (dst.size(0) == 0) return;
   const c10::cuda::CUDAGuard guard(src.device());
-  CFB_CHECK_RC(cfb_gather_rows(src.data_ptr(), src.stride(0) * es, idx.data_ptr<int>(),
-                               dst.data_ptr(), dst.stride(0) * es, dst.size(0),
-                               static_cast<int>(dst.size(1) * es), cur_stream()),
+  CFB_CHECK_RC(cfb_gather_rows(src.data_ptr(), src.stride(0) * es, src.size(0),
+                               idx.data_ptr<int>(), dst.data_ptr(), dst.stride(0) * es,
+                               dst.size(0), static_cast<int>(dst.size(1) * es),
+                               err_word(src.get_device()).data_ptr<int>(), cur_stream()),
                "gather_rows");
 }
 
@@ -452,8 +454,10 @@ void embedding_fwd(const Tensor& table, const Tensor& ids, Tensor& out) {
   TORCH_CHECK(table.is_contiguous() && out.is_contiguous(), "contiguous");
   if (ids.numel() == 0) return;
   const c10::cuda::CUDAGuard guard(table.device());
-  CFB_CHECK_RC(cfb_embedding_fwd(table.data_ptr(), reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()), out.data_ptr(),
-                                 ids.numel(), table.size(1), cur_stream()),
+  CFB_CHECK_RC(cfb_embedding_fwd(table.data_ptr(), table.size(0),
+                                 reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()),
+                                 out.data_ptr(), ids.numel(), table.size(1),
+                                 err_word(table.get_device()).data_ptr<int>(), cur_stream()),
                "embedding_fwd");
 }
 
@@ -465,7 +469,8 @@ void embedding_bwd(const Tensor& dy, const Tensor& ids, const c10::optional<Tens
   const c10::cuda::CUDAGuard guard(dy.device());
   CFB_CHECK_RC(cfb_embedding_bwd(dy.data_ptr(), reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()),
                                  reinterpret_cast<const int*>(opt_ptr<int>(id_rows)),
-                                 dtable.data_ptr<float>(), dy.size(0), dy.size(1), cur_stream()),
+                                 dtable.data_ptr<float>(), dtable.size(0), dy.size(0), dy.size(1),
+                                 err_word(dy.get_device()).data_ptr<int>(), cur_stream()),
                "embedding_bwd");
 }
 
@@ -477,7 +482,8 @@ void ce_fwd(const Tensor& logits, const Tensor& labels, Tensor& loss, Tensor& ls
   const c10::cuda::CUDAGuard guard(logits.device());
   CFB_CHECK_RC(cfb_ce_fwd(logits.data_ptr(), logits.stride(0), reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
                           loss.data_ptr<float>(), lse.data_ptr<float>(), logits.size(0),
-                          logits.size(1), cur_stream()),
+                          logits.size(1), err_word(logits.get_device()).data_ptr<int>(),
+                          cur_stream()),
                "ce_fwd");
 }
 

@@ -342,33 +342,52 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dh,
 
 // ---------------------------------------------------------------- gathers
 // dst[i, :] = src[idx[i], :]; row_bytes is a multiple of 16.  One warp per row.
+// An index outside [0, n) records kErrBounds in the status block; the caller skips the access.
+__device__ __forceinline__ bool index_ok(long long i, long long n, int* err) {
+  if (i >= 0 && i < n) return true;
+  if (err) atomicCAS(err, 0, kErrBounds);
+  return false;
+}
+
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, long long ld_src,
-                                   const int* __restrict__ idx, uint8_t* __restrict__ dst,
-                                   long long ld_dst, int rows, int row_bytes) {
+                                   long long src_rows, const int* __restrict__ idx,
+                                   uint8_t* __restrict__ dst, long long ld_dst, int rows,
+                                   int row_bytes, int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
-  const uint4* s = reinterpret_cast<const uint4*>(src + static_cast<long long>(idx[row]) * ld_src);
+  const long long i = idx[row];
   uint4* d = reinterpret_cast<uint4*>(dst + static_cast<long long>(row) * ld_dst);
+  if (!index_ok(i, src_rows, err)) {  // out-of-range row id: zero row instead of a stray read
+    for (int c = lane_id(); c < row_bytes / 16; c += 32) d[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(src + i * ld_src);
   for (int c = lane_id(); c < row_bytes / 16; c += 32) d[c] = s[c];
 }
 
-__global__ void embedding_fwd_kernel(const __nv_bfloat16* __restrict__ table,
+__global__ void embedding_fwd_kernel(const __nv_bfloat16* __restrict__ table, long long V,
                                      const long long* __restrict__ ids,
-                                     __nv_bfloat16* __restrict__ out, int rows, int H) {
+                                     __nv_bfloat16* __restrict__ out, int rows, int H, int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
-  const uint4* s = reinterpret_cast<const uint4*>(table + ids[row] * H);
+  const long long tok = ids[row];
   uint4* d = reinterpret_cast<uint4*>(out + static_cast<long long>(row) * H);
+  if (!index_ok(tok, V, err)) {  // token id outside the vocabulary: zero embedding
+    for (int c = lane_id(); c < H / 8; c += 32) d[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4* s = reinterpret_cast<const uint4*>(table + tok * H);
   for (int c = lane_id(); c < H / 8; c += 32) d[c] = s[c];
 }
 
 __global__ void embedding_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
                                      const long long* __restrict__ ids,
                                      const int* __restrict__ id_rows, float* __restrict__ dtable,
-                                     int rows, int H) {
+                                     long long V, int rows, int H, int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + warp_id();
   if (row >= rows) return;
   const long long tok = ids[id_rows ? id_rows[row] : row];
+  if (!index_ok(tok, V, err)) return;
   float* dst = dtable + tok * H;
   const __nv_bfloat16* src = dy + static_cast<long long>(row) * H;
   for (int c = lane_id() * 8; c < H; c += 256) {
@@ -424,7 +443,7 @@ __global__ void __launch_bounds__(256) ce_fwd_kernel(const __nv_bfloat16* __rest
                                                      long long ld,
                                                      const long long* __restrict__ labels,
                                                      float* __restrict__ loss,
-                                                     float* __restrict__ lse, int V) {
+                                                     float* __restrict__ lse, int V, int* err) {
   __shared__ float sm_m[8], sm_s[8];
   const int row = blockIdx.x;
   const __nv_bfloat16* lr = logits + static_cast<long long>(row) * ld;
@@ -447,7 +466,8 @@ __global__ void __launch_bounds__(256) ce_fwd_kernel(const __nv_bfloat16* __rest
     const float l = m + __logf(s);
     lse[row] = l;
     const long long lab = labels[row];
-    loss[row] = lab >= 0 ? (l - __bfloat162float(lr[lab])) : 0.f;
+    // negative labels are ignored positions; labels >= V are errors (recorded, loss 0)
+    loss[row] = (lab >= 0 && index_ok(lab, V, err)) ? (l - __bfloat162float(lr[lab])) : 0.f;
   }
 }
 
@@ -800,37 +820,39 @@ int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu
   return last_err();
 }
 
-int cfb_gather_rows(const void* src, long long ld_src, const int* idx, void* dst,
-                    long long ld_dst, int rows, int row_bytes, cudaStream_t st) {
+int cfb_gather_rows(const void* src, long long ld_src, long long src_rows, const int* idx,
+                    void* dst, long long ld_dst, int rows, int row_bytes, int* err,
+                    cudaStream_t st) {
   if (row_bytes % 16 || ld_src % 16 || ld_dst % 16) return -11;
   if (rows == 0) return 0;
-  gather_rows_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const uint8_t*>(src), ld_src, idx,
-                                                     static_cast<uint8_t*>(dst), ld_dst, rows,
-                                                     row_bytes);
+  gather_rows_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const uint8_t*>(src), ld_src,
+                                                     src_rows, idx, static_cast<uint8_t*>(dst),
+                                                     ld_dst, rows, row_bytes, err);
   return last_err();
 }
 
-int cfb_embedding_fwd(const void* table, const long long* ids, void* out, int rows, int H,
-                      cudaStream_t st) {
+int cfb_embedding_fwd(const void* table, long long V, const long long* ids, void* out, int rows,
+                      int H, int* err, cudaStream_t st) {
   if (H % 8) return -11;
-  embedding_fwd_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const bf16*>(table), ids,
-                                                       static_cast<bf16*>(out), rows, H);
+  embedding_fwd_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const bf16*>(table), V, ids,
+                                                       static_cast<bf16*>(out), rows, H, err);
   return last_err();
 }
 
 int cfb_embedding_bwd(const void* dy, const long long* ids, const int* id_rows, float* dtable,
-                      int rows, int H, cudaStream_t st) {
+                      long long V, int rows, int H, int* err, cudaStream_t st) {
   if (H % 8) return -11;
   if (rows == 0) return 0;
   embedding_bwd_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const bf16*>(dy), ids,
-                                                       id_rows, dtable, rows, H);
+                                                       id_rows, dtable, V, rows, H, err);
   return last_err();
 }
 
 int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float* loss,
-               float* lse, int rows, int V, cudaStream_t st) {
+               float* lse, int rows, int V, int* err, cudaStream_t st) {
   if (V % 8 || ld % 8) return -11;
-  ce_fwd_kernel<<<rows, 256, 0, st>>>(static_cast<const bf16*>(logits), ld, labels, loss, lse, V);
+  ce_fwd_kernel<<<rows, 256, 0, st>>>(static_cast<const bf16*>(logits), ld, labels, loss, lse, V,
+                                      err);
   return last_err();
 }
 
@@ -838,7 +860,7 @@ int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float*
 __global__ void __launch_bounds__(256) ce_combine_kernel(
     const float* __restrict__ pmax, const float* __restrict__ psum,
     const float* __restrict__ ptgt, int rows, int nt, const long long* __restrict__ labels,
-    float* __restrict__ loss, float* __restrict__ lse) {
+    long long V, float* __restrict__ loss, float* __restrict__ lse, int* err) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -854,15 +876,16 @@ __global__ void __launch_bounds__(256) ce_combine_kernel(
     const float l = m + __logf(s);
     lse[row] = l;
     const long long lab = labels[row];
-    loss[row] = lab >= 0 ? l - ptgt[row] : 0.f;
+    loss[row] = (lab >= 0 && index_ok(lab, V, err)) ? l - ptgt[row] : 0.f;
   }
 }
 
 int cfb_ce_combine(const float* pmax, const float* psum, const float* ptgt, int rows, int nt,
-                   const long long* labels, float* loss, float* lse, cudaStream_t st) {
+                   const long long* labels, long long V, float* loss, float* lse, int* err,
+                   cudaStream_t st) {
   if (rows <= 0) return 0;
-  ce_combine_kernel<<<(rows + 7) / 8, 256, 0, st>>>(pmax, psum, ptgt, rows, nt, labels, loss,
-                                                    lse);
+  ce_combine_kernel<<<(rows + 7) / 8, 256, 0, st>>>(pmax, psum, ptgt, rows, nt, labels, V, loss,
+                                                    lse, err);
   return last_err();
 }
 

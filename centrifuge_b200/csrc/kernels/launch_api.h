@@ -106,14 +106,18 @@ int cfb_rope(void* qkv, long long ld, const int* pos, const int* row_of, int row
 int cfb_swiglu_fwd(const void* gu, void* h, int rows, int F, cudaStream_t st);
 int cfb_swiglu_bwd(const void* dh, const void* gu, const int* gu_rows, void* dgu, void* h_out,
                    int rows, int F, cudaStream_t st);
-int cfb_gather_rows(const void* src, long long ld_src, const int* idx, void* dst,
-                    long long ld_dst, int rows, int row_bytes, cudaStream_t st);
-int cfb_embedding_fwd(const void* table, const long long* ids, void* out, int rows, int H,
-                      cudaStream_t st);
+// Index checks: a row id outside [0, src_rows), a token id outside [0, V) or a label >= V
+// records kErrBounds in `err` (the status block) and the access is skipped (gathered rows and
+// embeddings are zero, the loss is 0).
+int cfb_gather_rows(const void* src, long long ld_src, long long src_rows, const int* idx,
+                    void* dst, long long ld_dst, int rows, int row_bytes, int* err,
+                    cudaStream_t st);
+int cfb_embedding_fwd(const void* table, long long V, const long long* ids, void* out, int rows,
+                      int H, int* err, cudaStream_t st);
 int cfb_embedding_bwd(const void* dy, const long long* ids, const int* id_rows, float* dtable,
-                      int rows, int H, cudaStream_t st);
+                      long long V, int rows, int H, int* err, cudaStream_t st);
 int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float* loss,
-               float* lse, int rows, int V, cudaStream_t st);
+               float* lse, int rows, int V, int* err, cudaStream_t st);
 int cfb_ce_bwd(const void* logits, long long ld, const int* logit_rows, const long long* labels,
                const float* lse, const float* dloss, void* dlogits, long long ld_out, int rows,
                int V, long long vocab_start, cudaStream_t st);
@@ -186,7 +190,8 @@ int cfb_gemm_ce_grad(const void* X, long long ldx, const void* W, long long ldw,
 // lse[r] = M + log(sum_t psum[r, t] exp(pmax[r, t] - M)), M = max_t pmax[r, t];
 // loss[r] = lse[r] - ptgt[r] for labels[r] >= 0, else 0.
 int cfb_ce_combine(const float* pmax, const float* psum, const float* ptgt, int rows, int nt,
-                   const long long* labels, float* loss, float* lse, cudaStream_t st);
+                   const long long* labels, long long V, float* loss, float* lse, int* err,
+                   cudaStream_t st);
 
 // NVLink peer-memory gradient reduction (comm_sm100.cu).
 int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,

@@ -29,6 +29,7 @@ enum : int {
   kErrBadArgs = 16,
   kErrPeerWait = 32,
   kErrKeepCount = 64,
+  kErrBounds = 128,  // an index (token id, label, row id) outside its table: access skipped
 };
 constexpr int kStatusWords = 4;
 

@@ -79,7 +79,7 @@ def linear_fwd_ce(x: torch.Tensor, w: torch.Tensor, labels: torch.Tensor):
     loss, lse = torch.empty(M, **f32), torch.empty(M, **f32)
     k = kernels()
     k.gemm_ce_part(x, w, labels, pmax, psum, ptgt)
-    k.ce_combine(pmax, psum, ptgt, labels, loss, lse)
+    k.ce_combine(pmax, psum, ptgt, labels, N, loss, lse)
     return loss, lse
 
 

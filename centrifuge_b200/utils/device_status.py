@@ -27,6 +27,7 @@ ERROR_CODES = {
     16: "a kernel rejected its arguments",
     32: "a wait on another GPU ran out (peer flag not raised in time)",
     64: "a mask row did not keep the expected number of tokens",
+    128: "an index (token id, label or row id) was outside its table; the access was skipped",
 }
 
 

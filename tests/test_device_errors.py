@@ -129,3 +129,38 @@ def test_trainer_raises_one_step_after_a_failed_wait(short_peer_wait, tmp_path, 
     tr.train_step(batch, to_device=False)  # training can continue after handling it
     tr.status.check_now()
     assert not torch.equal(model.flat.data, before)
+
+
+@pytest.mark.gpu
+def test_out_of_range_indices_are_recorded_not_read():
+    """A token id past the vocabulary, a row id past the table and a label past the vocabulary
+    are recorded in the status word (kErrBounds) and skipped: zero rows / zero loss, no fault."""
+    from centrifuge_b200.ops import fused
+    from centrifuge_b200.ops._ext import kernels
+    k = kernels()
+    status = k.status_block(0)
+    status.zero_()
+    dev = torch.device("cuda", 0)
+    V, H = 64, 128
+    table = torch.randn(V, H, device=dev).bfloat16()
+    ids = torch.tensor([3, V, 5, V + 1000], device=dev)
+    out = fused.embedding_fwd(table, ids)
+    torch.cuda.synchronize()
+    assert int(status[0]) == 128
+    assert torch.equal(out[0], table[3]) and torch.equal(out[2], table[5])
+    assert float(out[1].float().abs().sum()) == 0.0 and float(out[3].float().abs().sum()) == 0.0
+    status.zero_()
+    rows = torch.tensor([1, -1, V], dtype=torch.int32, device=dev)
+    g = fused.gather_rows(table, rows)
+    torch.cuda.synchronize()
+    assert int(status[0]) == 128
+    assert torch.equal(g[0], table[1]) and float(g[1:].float().abs().sum()) == 0.0
+    status.zero_()
+    logits = torch.randn(4, V, device=dev).bfloat16()
+    labels = torch.tensor([1, V, -100, 2], device=dev)
+    loss, _ = fused.ce_fwd(logits, labels)
+    torch.cuda.synchronize()
+    assert int(status[0]) == 128
+    assert float(loss[1]) == 0.0 and float(loss[2]) == 0.0 and float(loss[0]) > 0.0
+    status.zero_()
+    torch.cuda.synchronize()
