@@ -61,6 +61,10 @@ def parse():
                          "centrifuge: filtered loss and filtered backward")
     ap.add_argument("--zero", type=int, default=2)
     ap.add_argument("--reducer", default="auto", choices=["auto", "nccl", "symm"])
+    ap.add_argument("--grad-mode", default="ring", choices=["ring", "full"],
+                    help="ring: partitioned ZeRO-2 gradients (bucket slots, reduce-scatter in "
+                         "every micro-batch); full: full fp32 local gradients reduced once per "
+                         "step (ZeRO-1 gradient memory)")
     ap.add_argument("--layers", type=int, default=None,
                     help="override the layer count (quick checks only; not a benchmark config)")
     ap.add_argument("--no-status", action="store_true",
@@ -137,14 +141,15 @@ def main():
     if world > 1 and args.reducer in ("auto", "symm"):
         try:
             from centrifuge_b200.parallel.symm import SymmReducer
-            reducer = SymmReducer.create(model.flat, group)
+            reducer = SymmReducer.create(model.flat, group, ring=args.grad_mode == "ring")
         except Exception as e:  # the NCCL baseline stays available
             if args.reducer == "symm":
                 raise
             if rank == 0:
                 print(f"symmetric-memory reducer unavailable ({e}); using NCCL", file=sys.stderr)
     opt = ZeroAdamW(model.flat, group=group, stage=args.zero, lr=1e-4, betas=(0.9, 0.95),
-                    eps=1e-8, weight_decay=0.0, grad_clip=1.0, reducer=reducer)
+                    eps=1e-8, weight_decay=0.0, grad_clip=1.0, reducer=reducer,
+                    grad_mode=args.grad_mode if args.zero == 2 else "full")
     drop = 0.0 if args.mode == "regular" else args.drop
     trainer = Trainer(model, opt, drop_rate=drop, grad_accum=args.ga, world_size=world,
                       filter_backward=args.mode == "centrifuge",
@@ -216,6 +221,8 @@ def main():
                        "micro_batch": args.mbs, "grad_accum": args.ga, "seq_len": args.seq,
                        "drop_rate": drop, "mode": args.mode,
                        "parallelism": f"zero{args.zero}-dp{world}",
+                       "grad_mode": opt.grad_mode,
+                       "grad_memory_gib": round(opt.grad_memory_bytes() / 2 ** 30, 3),
                        "layers": cfg.num_hidden_layers,
                        "reducer": (getattr(opt.reducer, "kind", type(opt.reducer).__name__)
                                    if opt.reducer else "none"),

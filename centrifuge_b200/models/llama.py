@@ -84,7 +84,7 @@ class LlamaCore(torch.nn.Module):
     def __init__(self, cfg: LlamaConfig, device="cuda", first: int = 0, last: Optional[int] = None,
                  has_embed: bool = True, has_head: bool = True, seed: int = 0,
                  init: bool = True, keep_logits: bool = False, dtype=torch.bfloat16,
-                 pad_to: int = 1):
+                 pad_to: int = 1, bucket_numel: int = 1 << 26):
         super().__init__()
         assert not cfg.tie_word_embeddings, "tied embeddings are not supported"
         self.cfg = cfg
@@ -96,8 +96,9 @@ class LlamaCore(torch.nn.Module):
         # CUDA: lm_head + cross entropy fused (no [T, V] logits kept between forward and
         # backward; the kept rows' logits are recomputed).  CFB_FUSED_CE=0 keeps the logits.
         self.fused_ce = os.environ.get("CFB_FUSED_CE", "1") != "0"
+        # with data parallelism (pad_to > 1) the layout is cut into reduce-scatter buckets
         self.flat = FlatParams(param_specs(cfg, self.layer_ids, has_embed, has_head), device,
-                               dtype=dtype, pad_to=pad_to)
+                               dtype=dtype, pad_to=pad_to, bucket_numel=bucket_numel)
         self.device = self.flat.device
         self.nh, self.nkv, self.hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         self.scale = 1.0 / math.sqrt(self.hd)

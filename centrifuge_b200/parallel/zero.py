@@ -10,14 +10,23 @@ range is cut into buckets; rank ``r`` owns chunk ``r`` of every bucket ("bucket-
 sharding), so a bucket is reduce-scattered as soon as the backward has finished it and each
 rank's optimizer shard is the concatenation of its chunks.
 
-Stage 2: when a bucket's gradients are final the bucket is reduced on a communication stream
-into the rank's fp32 gradient shard and its slice of the local gradient buffer is cleared.  By
-default this happens only in the backward of the last micro-batch of a step: the earlier
-micro-batches accumulate into the local fp32 buffer (which is full-size here anyway), so a step
-moves each gradient over NVLink once instead of ``grad_accum`` times, and the reduction still
-overlaps the last backward bucket by bucket.  ``reduce_every_micro=True`` reduces in every
-micro-batch's backward, as DeepSpeed's ZeRO-2 does.  Stage 1 accumulates the full local
-gradients over the micro-batches and reduces once at the boundary, without overlap.
+Stage 2 has two gradient modes.
+
+* ``grad_mode="ring"`` (partitioned, DeepSpeed ZeRO-2 semantics): no full-size gradient buffer.
+  The layout is cut into buckets that never split a parameter (``FlatParams.bucket_bounds``); a
+  bucket's gradients are written into one of ``ring_slots`` bucket-sized fp32 slots
+  (:class:`GradRing`), and as soon as the backward has finished the bucket it is reduce-scattered
+  into the rank's fp32 gradient shard, in every micro-batch.  A slot is reused only after its
+  reduction (and, over NVLink, every peer's read of it) has completed.  Gradient memory per rank
+  is the shard (1/W) plus ``ring_slots`` buckets.
+* ``grad_mode="full"`` (local accumulation, one reduction per step): every rank keeps a
+  full-size fp32 gradient buffer; the micro-batches of a step accumulate into it and the buckets
+  are reduced during the backward of the last micro-batch only, so a step moves each gradient
+  over NVLink once instead of ``grad_accum`` times.  Its gradient memory is that of ZeRO-1.
+  ``reduce_every_micro=True`` reduces in every micro-batch instead.
+
+Stage 1 accumulates the full local gradients over the micro-batches and reduces once at the
+boundary, without overlap.
 
 Step: global grad-norm (local sum of squares + one 4-byte all-reduce), clip coefficient computed
 on the device, fused AdamW on the fp32 master shard writing bf16 parameters, then a per-bucket
@@ -52,11 +61,86 @@ class Bucket:
         return self._own_lo
 
 
+def _buckets_per_unit(flat) -> int:
+    """Largest number of buckets whose gradients a model writes before it reports any of them
+    final: the parameters of one layer ("layers.<i>.*"), of the head (lm_head + norm), or the
+    embedding.  The gradient ring needs one slot more than that."""
+    units = {}
+    for name in flat.specs:
+        if name.startswith("layers."):
+            key = name.rsplit(".", 1)[0]
+        else:
+            key = "head" if name in ("lm_head", "norm") else name
+        o = flat.offsets[name]
+        for i, (lo, hi) in enumerate(flat.bucket_bounds):
+            if lo <= o < hi:
+                units.setdefault(key, set()).add(i)
+                break
+    return max((len(v) for v in units.values()), default=1)
+
+
 def _world(group):
     """(size, rank) of the data-parallel group; ``None`` means no data parallelism."""
     if group is None:
         return 1, 0
     return dist.get_world_size(group), dist.get_rank(group)
+
+
+class GradRing:
+    """Bucket-sized fp32 gradient slots of partitioned ZeRO-2.
+
+    Bucket ``b`` uses slot ``b % slots``.  :meth:`slot` hands out the bucket's slot on the
+    first access of a micro-batch, after running the ordering callable left by the slot's
+    previous bucket; :meth:`released` records that callable when the reduction of a bucket has
+    been issued.  Slots start zeroed and are cleared again on the communication stream right
+    after their reduction (once every reader is done), so the backward finds them zero without
+    a memset of its own.  A bucket that needs a slot whose previous bucket is not reduced yet
+    raises: the layer being differentiated spans more buckets than there are slots.
+    """
+
+    def __init__(self, buckets, slots: int, device, alloc=None):
+        self.sizes = [b.hi - b.lo for b in buckets]
+        self.slot_numel = max(self.sizes)
+        self.R = max(1, min(slots, len(buckets)))
+        n = self.R * self.slot_numel
+        self.buf = (alloc(n) if alloc is not None
+                    else torch.empty(n, dtype=torch.float32, device=device))
+        self.buf.zero_()
+        self.cur = {}
+        self.holder = [None] * self.R
+        self.pending = [False] * self.R
+        self.before_reuse = [None] * self.R
+
+    @property
+    def nbytes(self) -> int:
+        return self.buf.numel() * self.buf.element_size()
+
+    def begin_micro(self) -> None:
+        self.cur = {}
+
+    def _view(self, s: int, b: int) -> torch.Tensor:
+        return self.buf[s * self.slot_numel:s * self.slot_numel + self.sizes[b]]
+
+    def slot(self, b: int) -> torch.Tensor:
+        s = self.cur.get(b)
+        if s is None:
+            s = b % self.R
+            if self.pending[s]:
+                raise RuntimeError(
+                    f"gradient ring: bucket {b} needs slot {s}, which still holds bucket "
+                    f"{self.holder[s]} (not reduced yet); use more ring slots")
+            if self.before_reuse[s] is not None:
+                self.before_reuse[s]()
+                self.before_reuse[s] = None
+            self.cur[b] = s
+            self.holder[s] = b
+            self.pending[s] = True
+        return self._view(s, b)
+
+    def released(self, b: int, before_reuse) -> None:
+        s = self.cur[b]
+        self.pending[s] = False
+        self.before_reuse[s] = before_reuse
 
 
 class NcclReducer:
@@ -68,10 +152,17 @@ class NcclReducer:
         self.comm_dtype = comm_dtype
         self._send = None
         self._recv = None
+        self.ring = False  # partitioned gradients: the slot is cleared on its next use instead
 
     def reduce_bucket(self, idx: int, b, src_fp32: torch.Tensor, dst_fp32: torch.Tensor) -> None:
         self.reduce_scatter_acc(src_fp32, dst_fp32, 1.0)
-        src_fp32.zero_()
+        if not self.ring:
+            src_fp32.zero_()
+
+    def slot_reuse_wait(self, idx: int):
+        """Extra ordering before a ring slot that held bucket ``idx`` is written again (none:
+        the NCCL reduction is ordered by the communication stream's event)."""
+        return None
 
     def end_micro(self, flat) -> None:
         pass
@@ -99,16 +190,23 @@ class ZeroAdamW:
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0,
                  grad_clip: float = 1.0, bucket_numel: int = 1 << 26, reducer=None,
                  overlap: bool = True, norm_group=None, replicated_ranges=(),
-                 replication: Optional[int] = None, reduce_every_micro: bool = False):
+                 replication: Optional[int] = None, reduce_every_micro: bool = False,
+                 grad_mode: str = "full", ring_slots: int = 4):
         assert stage in (1, 2)
-        self.reduce_every_micro = reduce_every_micro
+        assert grad_mode in ("full", "ring")
+        self.W, self.rank = _world(group)
+        # partitioned gradients need more than one rank and the bucket-aligned layout
+        self.grad_mode = grad_mode if (stage == 2 and self.W > 1 and flat.bucket_bounds) else "full"
+        if grad_mode == "ring" and self.grad_mode != "ring" and self.W > 1:
+            raise ValueError("grad_mode='ring' needs stage 2 and a FlatParams built with "
+                             "bucket_numel (pad_to = data-parallel size)")
+        self.reduce_every_micro = reduce_every_micro or self.grad_mode == "ring"
         self._active = True  # this micro-batch's backward reduces buckets
         self.flat = flat
         self.group = group
         self.stage = stage
         self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
         self.grad_clip = grad_clip
-        self.W, self.rank = _world(group)
         self.device = flat.device
         self.step_count = 0
         self.overlap = overlap and self.W > 1 and flat.device.type == "cuda"
@@ -119,8 +217,10 @@ class ZeroAdamW:
         self.buckets: List[Bucket] = []
         off = 0
         lo = 0
+        bounds = list(flat.bucket_bounds) if (flat.bucket_bounds and self.W > 1) else None
         while lo < N:
-            hi = min(N, lo + bucket_numel)
+            hi = bounds[len(self.buckets)][1] if bounds else min(N, lo + bucket_numel)
+            assert (hi - lo) % quantum == 0, "bucket not divisible into aligned rank chunks"
             chunk = (hi - lo) // self.W
             b = Bucket(lo, hi, chunk, off)
             b._own_lo = lo + self.rank * chunk
@@ -144,6 +244,13 @@ class ZeroAdamW:
             self.param_out = torch.empty(self.shard_numel, dtype=flat.data.dtype, device=self.device)
         self.reducer = reducer if reducer is not None else (
             NcclReducer(group) if self.W > 1 else None)
+        self.ring = None
+        if self.grad_mode == "ring":
+            self.reducer.ring = True
+            slots = max(ring_slots, _buckets_per_unit(flat) + 1)
+            self.ring = GradRing(self.buckets, slots, self.device,
+                                 alloc=getattr(self.reducer, "alloc_ring", None))
+            flat.use_grad_ring(self.ring)
         self._coef = torch.ones(1, **f32)
         self._norm = torch.zeros(1, **f32)
         self._sumsq = torch.zeros(148 * 4, **f32)
@@ -173,6 +280,8 @@ class ZeroAdamW:
         """Start a micro-batch; ``last`` marks the last one before :meth:`step`."""
         self._ready = 0
         self._active = last or self.reduce_every_micro
+        if self.ring is not None:
+            self.ring.begin_micro()
 
     def on_grads_ready(self, lo: int, hi: int) -> None:
         if not self._active:
@@ -183,16 +292,40 @@ class ZeroAdamW:
             self._ready += 1
 
     def _reduce_bucket(self, b: Bucket) -> None:
-        src = self.flat.grad[b.lo:b.hi]
-        dst = self.grad_shard[b.shard_off:b.shard_off + b.chunk]
         idx = self.buckets.index(b) if not hasattr(b, "idx") else b.idx
+        # a bucket without gradients in this micro-batch still takes part (zero slot)
+        src = self.ring.slot(idx) if self.ring is not None else self.flat.grad[b.lo:b.hi]
+        dst = self.grad_shard[b.shard_off:b.shard_off + b.chunk]
+        ev = None
+
+        def reduce_and_clear():
+            self.reducer.reduce_bucket(idx, b, src, dst)
+            if self.ring is not None:
+                # clear the slot for its next bucket once every reader (over NVLink: every
+                # peer) is done with it, off the backward's stream
+                peers = self.reducer.slot_reuse_wait(idx)
+                if peers is not None:
+                    peers()
+                src.zero_()
+
         if self._comm_stream is not None:
             cur = torch.cuda.current_stream(self.device)
             self._comm_stream.wait_stream(cur)
             with torch.cuda.stream(self._comm_stream):
-                self.reducer.reduce_bucket(idx, b, src, dst)
+                reduce_and_clear()
+                if self.ring is not None:
+                    ev = torch.cuda.Event()
+                    ev.record()
         else:
-            self.reducer.reduce_bucket(idx, b, src, dst)
+            reduce_and_clear()
+        if self.ring is not None:
+            dev = self.device
+
+            def before_reuse(ev=ev):
+                if ev is not None:
+                    torch.cuda.current_stream(dev).wait_event(ev)
+
+            self.ring.released(idx, before_reuse)
 
     def end_micro(self) -> None:
         """Finish the micro-batch: reduce what is left (stage 2) and join the comm stream."""
@@ -219,6 +352,13 @@ class ZeroAdamW:
             self.grad_shard.zero_()
             if self.stage == 1:
                 self.flat.grad.zero_()
+
+    def grad_memory_bytes(self) -> int:
+        """Device bytes held for gradients on this rank (local buffer or ring + fp32 shard)."""
+        shard = 0 if self.W == 1 else self.grad_shard.numel() * 4
+        if self.ring is not None:
+            return self.ring.nbytes + shard
+        return self.flat.grad.numel() * self.flat.grad.element_size() + shard
 
     def _reduce_all_stage1(self) -> None:
         for b in self.buckets:

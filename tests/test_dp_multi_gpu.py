@@ -27,23 +27,31 @@ def _worker(rank, world, port, q):
         cfg = tiny_llama_test(layers=2, hidden=256, heads=4, kv_heads=2, ffn=512, vocab=1024,
                               head_dim=64)
         results = {}
-        for kind in ("nccl", "symm"):
-            model = NativeLlamaForCausalLM(cfg, device="cuda", seed=0, pad_to=world)
+        # (reducer, gradient mode): full local fp32 gradients reduced once per step, or
+        # partitioned ZeRO-2 gradients in a ring of bucket slots reduced every micro-batch
+        for kind, mode in (("nccl", "full"), ("symm", "full"), ("nccl", "ring"),
+                           ("symm", "ring")):
+            model = NativeLlamaForCausalLM(cfg, device="cuda", seed=0, pad_to=world,
+                                           bucket_numel=1 << 16)
             g = dist.group.WORLD
-            red = (SymmReducer.create(model.flat, g) if kind == "symm"
+            red = (SymmReducer.create(model.flat, g, ring=mode == "ring") if kind == "symm"
                    else NcclReducer(g, comm_dtype=torch.float32))
             opt = ZeroAdamW(model.flat, group=g, stage=2, lr=1e-3, bucket_numel=1 << 16,
-                            reducer=red)
+                            reducer=red, grad_mode=mode)
+            assert (model.flat.grad is None) == (mode == "ring")
             tr = Trainer(model, opt, drop_rate=0.5, grad_accum=2, world_size=world)
             data = SyntheticTokenData(cfg.vocab_size, 2, 128, seed=1, rank=rank)
             for _ in range(2):
                 tr.train_step([data.sample() for _ in range(2)])
+            tr.status.check_now()
             torch.cuda.synchronize()
             if kind == "symm":
                 red.check()
                 results["kind"] = red.kind
-            results[kind] = model.flat.data.float().cpu()
-        err = ((results["symm"] - results["nccl"]).norm() / results["nccl"].norm()).item()
+            results[(kind, mode)] = model.flat.data.float().cpu()
+        ref = results[("nccl", "full")]
+        err = max(((results[k] - ref).norm() / ref.norm()).item()
+                  for k in results if k not in ("kind", ("nccl", "full")))
         q.put((rank, err, results.get("kind")))
     finally:
         dist.destroy_process_group()
