@@ -12,8 +12,8 @@ Per micro-batch the last stage computes the per-token loss, the selection mask a
 backward.  The mask is sent back with the gradient, so earlier stages build the same kept-row
 layout; backward point-to-point messages carry only the (padded) kept rows ``[C, H]`` of the
 sequence shard, forward messages the full shard ``[T/TP, H]``.  Sends are non-blocking
-(NCCL / gloo ``isend``), receives are waited in schedule order, which keeps the 1F1B order
-deadlock-free.
+(NCCL / gloo ``isend``); receives of a known shape are posted one schedule slot ahead of their
+use (a forward's input, a backward's mask) so that the transfer overlaps the slot before.
 """
 from __future__ import annotations
 
@@ -73,6 +73,7 @@ class PipelineTrainer:
         self.last = groups.stage == groups.pp - 1
         self.device = core.device
         self._sends: List = []
+        self._pending = {}  # posted receives: (kind, micro-batch) -> (work, tensor)
         # device errors (bounded waits that ran out, bad masks) surface one step late
         self.status = None
         if check_device_errors and torch.device(self.device).type == "cuda":
@@ -80,13 +81,29 @@ class PipelineTrainer:
             self.status = DeviceStatus(self.device)
 
     # ------------------------------------------------------------------ p2p
+    # Receives whose shape is known in advance are posted one schedule slot ahead, so the
+    # transfer runs under the compute of the slot before: a forward's input activations are
+    # posted when the previous forward starts (the previous stage sends them before it needs
+    # anything of this micro-batch's backward), a backward's mask right after the send of the
+    # forward output that precedes that backward.  Per neighbour the posting order equals the
+    # neighbour's send order, so in-order p2p streams (NCCL) cannot deadlock.
     def _isend(self, t: torch.Tensor, dst: int) -> None:
         self._sends.append((dist.isend(t.contiguous(), dst), t))
 
-    def _recv(self, shape, dtype, src: int) -> torch.Tensor:
-        t = torch.empty(shape, dtype=dtype, device=self.device)
-        dist.irecv(t, src).wait()
+    def _post(self, key, shape, dtype, src: int) -> None:
+        if key not in self._pending:
+            t = torch.empty(shape, dtype=dtype, device=self.device)
+            self._pending[key] = (dist.irecv(t, src), t)
+
+    def _take(self, key, shape, dtype, src: int) -> torch.Tensor:
+        self._post(key, shape, dtype, src)
+        w, t = self._pending.pop(key)
+        w.wait()
         return t
+
+    def _fwd_shape(self, batch):
+        B, S = batch[0].shape
+        return (B * S // self.g.tp, self.core.cfg.hidden_size)
 
     def _drain_sends(self) -> None:
         for w, _ in self._sends:
@@ -94,18 +111,22 @@ class PipelineTrainer:
         self._sends.clear()
 
     # ------------------------------------------------------------------ stages
-    def _forward(self, batch):
-        ids, ref = batch
+    def _forward(self, i: int, batches, prefetch_bwd: int = -1):
+        ids, ref = batches[i]
         B, S = ids.shape
-        T = B * S
-        H = self.core.cfg.hidden_size
+        dt = self.core.flat.data.dtype
         hidden = None
         if not self.first:
-            hidden = self._recv((T // self.g.tp, H), self.core.flat.data.dtype, self.g.prev)
+            hidden = self._take(("f", i), self._fwd_shape(batches[i]), dt, self.g.prev)
+            if i + 1 < len(batches):
+                self._post(("f", i + 1), self._fwd_shape(batches[i + 1]), dt, self.g.prev)
         out = self.core(input_ids=ids, hidden=hidden, batch_shape=(B, S))
         if not self.last:
             self._isend(out.hidden.detach(), self.g.next)
-            return {"ids": ids, "out": out, "B": B, "S": S}
+            if prefetch_bwd >= 0:
+                pb, ps = batches[prefetch_bwd][0].shape
+                self._post(("m", prefetch_bwd), (pb, ps), torch.long, self.g.next)
+            return {"i": i, "ids": ids, "out": out, "B": B, "S": S}
         mask = torch.ones(B, S, dtype=torch.long, device=self.device)
         if self.drop_rate > 0:
             loss, mask = token_filter_loss(ids, None, mask, ref, self.strategy, self.drop_rate,
@@ -115,7 +136,7 @@ class PipelineTrainer:
         else:
             loss = token_filter_loss(ids, None, mask, None, None, None, True,
                                      per_token_loss=out.token_loss)
-        return {"ids": ids, "loss": loss, "mask": mask, "B": B, "S": S}
+        return {"i": i, "ids": ids, "loss": loss, "mask": mask, "B": B, "S": S}
 
     def _backward(self, st):
         B, S = st["B"], st["S"]
@@ -126,7 +147,7 @@ class PipelineTrainer:
             dx = self.core.pending_input_grad
             mask = st["mask"]
         else:
-            mask = self._recv((B, S), torch.long, self.g.next)
+            mask = self._take(("m", st["i"]), (B, S), torch.long, self.g.next)
             filtered = bool(self.drop_rate > 0)
             if filtered and self.strategy == "fixed":
                 # every row keeps S - k tokens, known statically: no host read of the mask
@@ -134,7 +155,7 @@ class PipelineTrainer:
             state = state_for_mask(mask) if filtered else None
             lay = KeptLayout(state.rows if state is not None else None, B * S,
                              self.core.tp, self.device)
-            grad = self._recv((lay.C, H), self.core.flat.data.dtype, self.g.next)
+            grad = self._take(("g", st["i"]), (lay.C, H), self.core.flat.data.dtype, self.g.next)
             fn = st["out"].hidden.grad_fn
             sv = fn.saved if fn is not None else None
             dx = self.core._backward_impl(sv, grad, state)
@@ -151,15 +172,14 @@ class PipelineTrainer:
         rank).  Returns the mean loss on the last stage, None elsewhere."""
         M = len(batches)
         warm = min(self.g.pp - self.g.stage - 1, M)
+        self._pending = {}
         q = deque()
         losses = []
-        fi = 0
-        for _ in range(warm):
-            q.append(self._forward(batches[fi]))
-            fi += 1
-        for _ in range(M - warm):
-            q.append(self._forward(batches[fi]))
-            fi += 1
+        for fi in range(warm):
+            q.append(self._forward(fi, batches))
+        for k in range(M - warm):
+            # the backward that follows this forward is micro-batch k: post its mask now
+            q.append(self._forward(warm + k, batches, prefetch_bwd=k))
             l = self._backward(q.popleft())
             if l is not None:
                 losses.append(l.detach())
@@ -167,6 +187,7 @@ class PipelineTrainer:
             l = self._backward(q.popleft())
             if l is not None:
                 losses.append(l.detach())
+        assert not self._pending, f"unconsumed pipeline receives: {sorted(self._pending)}"
         self._drain_sends()
         self.core.reduce_replicated_grads()
         self.opt.step(grad_scale=1.0 / M)

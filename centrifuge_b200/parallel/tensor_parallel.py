@@ -82,6 +82,13 @@ class KeptLayout:
         self.identity = False
         rows = rows.to(device=device, dtype=torch.int64)
         Tk = rows.numel()
+        if P == 1:  # one shard: the padded layout is the compact one, no host read
+            self.rows = rows.to(torch.int32)
+            self.Tk, self.C, self.count, self.counts = Tk, Tk, Tk, [Tk]
+            self.local = self.rows
+            self.c2p = torch.arange(Tk, **i32)
+            self.p2c = self.c2p
+            return
         owner = rows // shard
         counts = torch.bincount(owner, minlength=P)
         prefix = torch.cumsum(counts, 0) - counts

@@ -257,6 +257,7 @@ class ZeroAdamW:
         self._sumsq_total = torch.zeros(1, **f32)
         self._comm_stream = torch.cuda.Stream(device=self.device) if self.overlap else None
         self._ready = 0  # buckets reduced in the current micro-batch
+        self._last = True  # the current micro-batch is the last before step()
         self.grad_scale = 1.0
         # Model-parallel group whose ranks hold different shards of the model: the grad-norm
         # sums over it; ``replicated_ranges`` (flat [lo, hi) ranges of parameters replicated on
@@ -279,6 +280,7 @@ class ZeroAdamW:
     def begin_micro(self, last: bool = True) -> None:
         """Start a micro-batch; ``last`` marks the last one before :meth:`step`."""
         self._ready = 0
+        self._last = last
         self._active = last or self.reduce_every_micro
         if self.ring is not None:
             self.ring.begin_micro()
@@ -334,7 +336,11 @@ class ZeroAdamW:
         if self.stage == 2:
             self.on_grads_ready(0, self.flat.numel)
             self._finish_reducer()
-        if self._comm_stream is not None:
+        if self._comm_stream is not None and (self._last or self.ring is None):
+            # The next micro-batch's forward touches neither the ring nor the shard: with
+            # partitioned gradients the tail of this micro-batch's reductions (the first
+            # layers and the embedding) keeps running under it.  Ring slots are ordered by
+            # their own events, the optimizer step joins after the last micro-batch.
             torch.cuda.current_stream(self.device).wait_stream(self._comm_stream)
 
     def _finish_reducer(self) -> None:
