@@ -462,11 +462,31 @@ void embedding_fwd(const Tensor& table, const Tensor& ids, Tensor& out) {
 }
 
 void embedding_bwd(const Tensor& dy, const Tensor& ids, const c10::optional<Tensor>& id_rows,
-                   Tensor& dtable) {
+                   Tensor& dtable, bool deterministic) {
   TORCH_CHECK(dtable.scalar_type() == at::kFloat && dtable.is_contiguous(), "dtable fp32");
   TORCH_CHECK(dy.is_contiguous() && ids.scalar_type() == at::kLong, "dy/ids");
   if (dy.size(0) == 0) return;
   const c10::cuda::CUDAGuard guard(dy.device());
+  if (deterministic) {
+    // each row's token, a stable sort by token, then one warp per run of equal tokens
+    int* err = err_word(dy.get_device()).data_ptr<int>();
+    Tensor tok = at::empty({dy.size(0)}, ids.options());
+    CFB_CHECK_RC(cfb_row_tokens(reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()),
+                                ids.numel(), reinterpret_cast<const int*>(opt_ptr<int>(id_rows)),
+                                reinterpret_cast<long long*>(tok.data_ptr<int64_t>()),
+                                dy.size(0), err, cur_stream()),
+                 "row_tokens");
+    auto sorted = at::sort(tok, /*stable=*/true, /*dim=*/0, /*descending=*/false);
+    const Tensor& stok = std::get<0>(sorted);
+    const Tensor& order = std::get<1>(sorted);
+    CFB_CHECK_RC(cfb_embedding_bwd_sorted(
+                     dy.data_ptr(), reinterpret_cast<const long long*>(stok.data_ptr<int64_t>()),
+                     reinterpret_cast<const long long*>(order.data_ptr<int64_t>()),
+                     dtable.data_ptr<float>(), dtable.size(0), dy.size(0), dy.size(1), err,
+                     cur_stream()),
+                 "embedding_bwd_sorted");
+    return;
+  }
   CFB_CHECK_RC(cfb_embedding_bwd(dy.data_ptr(), reinterpret_cast<const long long*>(ids.data_ptr<int64_t>()),
                                  reinterpret_cast<const int*>(opt_ptr<int>(id_rows)),
                                  dtable.data_ptr<float>(), dtable.size(0), dy.size(0), dy.size(1),
@@ -810,7 +830,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("gather_rows", &gather_rows);
   m.def("embedding_fwd", &embedding_fwd);
-  m.def("embedding_bwd", &embedding_bwd);
+  m.def("embedding_bwd", &embedding_bwd, py::arg("dy"), py::arg("ids"), py::arg("id_rows"),
+        py::arg("dtable"), py::arg("deterministic") = true);
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd", &ce_bwd, py::arg("logits"), py::arg("rows"), py::arg("labels"),
         py::arg("lse"), py::arg("dloss"), py::arg("dlogits"), py::arg("vocab_start") = 0);

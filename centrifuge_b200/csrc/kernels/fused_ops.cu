@@ -398,6 +398,50 @@ __global__ void embedding_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
   }
 }
 
+// Deterministic embedding gradient, in two steps around a stable sort of the rows by token:
+//   1. row_tokens: tok[r] = ids[id_rows[r]] (or ids[r]), -1 for a row id outside ids;
+//   2. (stable sort of tok on the host side, giving sorted tokens and their source rows)
+//   3. embedding_bwd_sorted: the first warp of each run of equal tokens sums the run's rows of
+//      dy in ascending row order and adds the sum into the table row, which no other warp
+//      touches.  The result does not depend on scheduling (no atomics), so two runs give the
+//      same bits.  Token ids outside [0, V) record kErrBounds and are skipped.
+__global__ void row_tokens_kernel(const long long* __restrict__ ids, long long n_ids,
+                                  const int* __restrict__ id_rows, long long* __restrict__ tok,
+                                  int rows, int* err) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const long long i = id_rows ? id_rows[r] : r;
+  tok[r] = index_ok(i, n_ids, err) ? ids[i] : -1;
+}
+
+__global__ void embedding_bwd_sorted_kernel(const __nv_bfloat16* __restrict__ dy,
+                                            const long long* __restrict__ stok,
+                                            const long long* __restrict__ order,
+                                            float* __restrict__ dtable, long long V, int rows,
+                                            int H, int* err) {
+  const int i = blockIdx.x * (blockDim.x / 32) + warp_id();
+  if (i >= rows) return;
+  const long long tok = stok[i];
+  if (i > 0 && stok[i - 1] == tok) return;  // not the first row of its run
+  if (!index_ok(tok, V, tok < 0 ? nullptr : err)) return;  // -1: row id already reported
+  float* dst = dtable + tok * H;
+  for (int c = lane_id() * 8; c < H; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = i; j < rows && stok[j] == tok; ++j) {
+      float f[8];
+      load8(dy + order[j] * H + c, f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] += f[k];
+    }
+    float4* d = reinterpret_cast<float4*>(dst + c);
+    float4 a = d[0], b = d[1];
+    a.x += acc[0]; a.y += acc[1]; a.z += acc[2]; a.w += acc[3];
+    b.x += acc[4]; b.y += acc[5]; b.z += acc[6]; b.w += acc[7];
+    d[0] = a;
+    d[1] = b;
+  }
+}
+
 // ---------------------------------------------------------------- cross entropy
 __device__ __forceinline__ void block_max_sum(float& m, float& s, float* sm_m, float* sm_s) {
   // combine (max, sum-of-exp) pairs across the block (blockDim = 256)
@@ -845,6 +889,23 @@ int cfb_embedding_bwd(const void* dy, const long long* ids, const int* id_rows, 
   if (rows == 0) return 0;
   embedding_bwd_kernel<<<(rows + 7) / 8, 256, 0, st>>>(static_cast<const bf16*>(dy), ids,
                                                        id_rows, dtable, V, rows, H, err);
+  return last_err();
+}
+
+int cfb_row_tokens(const long long* ids, long long n_ids, const int* id_rows, long long* tok,
+                   int rows, int* err, cudaStream_t st) {
+  if (rows == 0) return 0;
+  row_tokens_kernel<<<(rows + 255) / 256, 256, 0, st>>>(ids, n_ids, id_rows, tok, rows, err);
+  return last_err();
+}
+
+int cfb_embedding_bwd_sorted(const void* dy, const long long* sorted_tok,
+                             const long long* order, float* dtable, long long V, int rows, int H,
+                             int* err, cudaStream_t st) {
+  if (H % 8 || (reinterpret_cast<uintptr_t>(dtable) & 15)) return -11;
+  if (rows == 0) return 0;
+  embedding_bwd_sorted_kernel<<<(rows + 7) / 8, 256, 0, st>>>(
+      static_cast<const bf16*>(dy), sorted_tok, order, dtable, V, rows, H, err);
   return last_err();
 }
 

@@ -116,6 +116,14 @@ int cfb_embedding_fwd(const void* table, long long V, const long long* ids, void
                       int H, int* err, cudaStream_t st);
 int cfb_embedding_bwd(const void* dy, const long long* ids, const int* id_rows, float* dtable,
                       long long V, int rows, int H, int* err, cudaStream_t st);
+// Deterministic embedding gradient: cfb_row_tokens gathers each dy row's token (-1 for a row
+// id outside ids), the caller sorts them stably, cfb_embedding_bwd_sorted sums every run of
+// equal tokens in row order into its table row (no atomics).
+int cfb_row_tokens(const long long* ids, long long n_ids, const int* id_rows, long long* tok,
+                   int rows, int* err, cudaStream_t st);
+int cfb_embedding_bwd_sorted(const void* dy, const long long* sorted_tok,
+                             const long long* order, float* dtable, long long V, int rows, int H,
+                             int* err, cudaStream_t st);
 int cfb_ce_fwd(const void* logits, long long ld, const long long* labels, float* loss,
                float* lse, int rows, int V, int* err, cudaStream_t st);
 int cfb_ce_bwd(const void* logits, long long ld, const int* logit_rows, const long long* labels,

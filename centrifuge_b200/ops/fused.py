@@ -115,13 +115,16 @@ def embedding_fwd(table: torch.Tensor, ids: torch.Tensor, out: Optional[torch.Te
 
 
 def embedding_bwd(dy: torch.Tensor, ids: torch.Tensor, dtable: torch.Tensor,
-                  id_rows: Optional[torch.Tensor] = None):
+                  id_rows: Optional[torch.Tensor] = None, deterministic: bool = True):
+    """``dtable[ids[id_rows[r]]] += dy[r]``.  ``deterministic``: rows are sorted by token and
+    each token's rows are summed in row order by one warp (same bits on every run); otherwise
+    fp32 atomics, whose summation order varies from run to run."""
     ids = ids.reshape(-1)
     if not dy.is_cuda:
         sel = ids if id_rows is None else ids[id_rows.long()]
         dtable.index_add_(0, sel, dy.float())
         return dtable
-    kernels().embedding_bwd(dy, ids.contiguous(), id_rows, dtable)
+    kernels().embedding_bwd(dy, ids.contiguous(), id_rows, dtable, deterministic)
     return dtable
 
 

@@ -163,4 +163,15 @@ def test_out_of_range_indices_are_recorded_not_read():
     assert int(status[0]) == 128
     assert float(loss[1]) == 0.0 and float(loss[2]) == 0.0 and float(loss[0]) > 0.0
     status.zero_()
+    # embedding gradient: token V (out of range) and row id 9 (past ids) are skipped
+    dy = torch.randn(3, H, device=dev).bfloat16()
+    for det in (True, False):
+        dt = torch.zeros(V, H, device=dev)
+        fused.embedding_bwd(dy, ids, dt, torch.tensor([0, 1, 9], dtype=torch.int32, device=dev),
+                            deterministic=det)
+        torch.cuda.synchronize()
+        assert int(status[0]) == 128
+        assert torch.equal(dt[3], dy[0].float()) and float(dt.abs().sum()) == float(
+            dy[0].float().abs().sum())
+        status.zero_()
     torch.cuda.synchronize()

@@ -172,6 +172,32 @@ def test_gather_embedding():
     assert rel_err(dt, want) < 1e-5
 
 
+
+def test_embedding_bwd_deterministic():
+    """Sorted-run embedding gradient: matches the fp32 scatter-add, repeated tokens included,
+    and gives the same bits on every call (the atomic variant does not promise that)."""
+    torch.manual_seed(15)
+    V, H, T, R = 50, 2048, 4096, 3000
+    ids = torch.randint(0, V, (T,), device=dev)  # ~60 rows per token: long runs
+    rows = torch.randperm(T, device=dev)[:R].sort().values.int()
+    dy = torch.randn(R, H, device=dev).bfloat16()
+    base = torch.randn(V, H, device=dev)
+    want = base.clone().index_add_(0, ids[rows.long()], dy.float())
+    outs = []
+    for _ in range(2):
+        dt = base.clone()
+        fused.embedding_bwd(dy, ids, dt, rows, deterministic=True)
+        outs.append(dt)
+    assert rel_err(outs[0], want) < 1e-6
+    assert torch.equal(outs[0], outs[1])
+    dt = base.clone()
+    fused.embedding_bwd(dy, ids, dt, rows, deterministic=False)
+    assert rel_err(dt, want) < 1e-6
+    # without a row map
+    dt = base.clone()
+    fused.embedding_bwd(dy, ids[:R], dt)
+    assert rel_err(dt, base.clone().index_add_(0, ids[:R], dy.float())) < 1e-6
+
 def test_cross_entropy():
     torch.manual_seed(6)
     T, V = 64, 32000
