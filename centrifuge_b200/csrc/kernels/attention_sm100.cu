@@ -30,6 +30,7 @@
 #include "launch_api.h"
 
 #include <math_constants.h>
+#include <cstdlib>
 
 namespace cfb {
 namespace attn_tc {
@@ -546,6 +547,414 @@ __global__ void __launch_bounds__(Smem<HD>::THREADS, 1)
   }
 }
 
+// ------------------------------------------------------------------ two-tile ("ping-pong") form
+// Work item: one 128-query block of TWO heads of the same GQA group (heads 2 hp, 2 hp + 1 share
+// their K/V head, so both query tiles walk the same K_j / V_j tiles and the same causal range).
+// Each tile has its own softmax group of four warps (one per TMEM lane quadrant; a thread owns a
+// whole query row and all 128 keys of a step) and its own S and O in TMEM:
+//   TMEM columns  [0, 128) S_A (P_A packed bf16 into the first 64)   [128, 256) S_B
+//                 [256, 256 + HD) O_A                                 [256 + HD, 256 + 2 HD) O_B
+// MMA issue order per key step j:  P_A V_j, S_A(j+1) = Q_A K_{j+1}^T, P_B V_j, S_B(j+1).  Tile
+// A's softmax of step j+1 thus runs while the tensor cores do tile B's P V and next scores, and
+// the other way round, so the exponentials of one tile overlap the other tile's MMAs.  A tile's
+// S is rewritten only by the MMA after its own P V (issued in order by one thread), and the
+// scores of step j being ready imply that P V of step j-1 is complete, which makes the O
+// rescale of step j safe without a further wait.
+template <int HD>
+struct SmemPP {
+  static constexpr int QBUF = HD == 64 ? 2 : 1;       // items whose Q tiles are in flight
+  static constexpr int KV_STAGES = HD == 64 ? 4 : 2;  // slots of each of the K and V rings
+  static constexpr int CHUNK = BM * 128;              // 128 rows x 128 B (64 bf16)
+  static constexpr int Q_TILE = (HD / 64) * CHUNK;    // one head's Q [128 x HD]
+  static constexpr int Q_BYTES = 2 * Q_TILE;          // both tiles of an item
+  static constexpr int KV_TILE = (HD / 64) * CHUNK;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + QBUF * Q_BYTES;
+  static constexpr int OFF_V = OFF_K + KV_STAGES * KV_TILE;
+  static constexpr int OFF_BAR = OFF_V + KV_STAGES * KV_TILE;
+  static constexpr int THREADS = 64 + 2 * 128;        // TMA + MMA warps, 2 x 4 softmax warps
+  static constexpr int BYTES = OFF_BAR + 256 + 1024;
+  static_assert(KV_STAGES <= MAX_RING && QBUF <= 2, "rings");
+  static_assert(BYTES <= 232448, "shared memory per CTA");
+};
+
+struct BarsPP {
+  uint64_t q_full[2], q_empty[2], k_full[MAX_RING], k_empty[MAX_RING], v_full[MAX_RING],
+      v_empty[MAX_RING], s_full[2], p_ready[2], o_done[2], o_free[2], drain;
+  int item[2];
+  uint32_t tmem_slot;
+  int abort;
+};
+
+// item id -> (query block, first head of the pair, batch); heaviest query blocks first
+__device__ __forceinline__ Item decode_pp(int id, const Params& p) {
+  const int nhp = p.nh >> 1;
+  Item t;
+  t.qb = p.nqb - 1 - id / (nhp * p.B);
+  const int rem = id % (nhp * p.B);
+  t.h = 2 * (rem % nhp);
+  t.b = rem / nhp;
+  const int last_q = min(p.S, (t.qb + 1) * BM) - 1;
+  t.nkb = last_q / BN + 1;
+  return t;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(SmemPP<HD>::THREADS, 1)
+    attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
+  using L = SmemPP<HD>;
+  constexpr int QBUF = L::QBUF, KVS = L::KV_STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  BarsPP* bar = reinterpret_cast<BarsPP*>(smem + L::OFF_BAR);
+  volatile int* abort_flag = &bar->abort;
+  volatile int* item_slot = bar->item;
+  const int warp = warp_id(), lane = lane_id();
+  const int group = p.nh / p.nkv;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < QBUF; ++i) {
+      mbar_init(smem_u32(&bar->q_full[i]), 1);
+      mbar_init(smem_u32(&bar->q_empty[i]), 1);
+    }
+    for (int s = 0; s < KVS; ++s) {
+      mbar_init(smem_u32(&bar->k_full[s]), 1);
+      mbar_init(smem_u32(&bar->k_empty[s]), 1);
+      mbar_init(smem_u32(&bar->v_full[s]), 1);
+      mbar_init(smem_u32(&bar->v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&bar->s_full[t]), 1);
+      mbar_init(smem_u32(&bar->p_ready[t]), 4);
+      mbar_init(smem_u32(&bar->o_done[t]), 1);
+      mbar_init(smem_u32(&bar->o_free[t]), 4);
+    }
+    mbar_init(smem_u32(&bar->drain), 1);
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tm);
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bar->tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_slot;
+  const uint32_t sbase = smem_u32(smem);
+  constexpr uint32_t kOCol = 2 * BN;  // O_A, O_B after the two S tiles
+  static_assert(2 * BN + 2 * HD <= 512, "TMEM columns");
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ scheduler + TMA producer
+      int k = 0, gk = 0, gv = 0;
+      bool ok = true;
+      for (; ok; ++k) {
+        const int qs = k % QBUF;
+        if (!mbar_wait(smem_u32(&bar->q_empty[qs]), ((k / QBUF) & 1) ^ 1, abort_flag, p.err,
+                       kErrWaitProducer)) {
+          ok = false;
+          break;
+        }
+        int id = atomicAdd(p.work, 1);
+        if (id >= p.n_items) id = -1;
+        item_slot[qs] = id;
+        if (id < 0) {
+          mbar_arrive(smem_u32(&bar->q_full[qs]));
+          ++k;
+          break;
+        }
+        const Item t = decode_pp(id, p);
+        const int row0 = t.b * p.S;
+        const int kvh = t.h / group;
+        const int kcol = (p.nh + kvh) * HD, vcol = (p.nh + p.nkv + kvh) * HD;
+        const uint32_t qfb = smem_u32(&bar->q_full[qs]);
+        mbar_arrive_expect_tx(qfb, L::Q_BYTES);
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt)
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_load_2d(sbase + L::OFF_Q + qs * L::Q_BYTES + tt * L::Q_TILE + c * L::CHUNK, &tm,
+                        qfb, (t.h + tt) * HD + c * 64, row0 + t.qb * BM);
+        // K_0, K_1, V_0, K_2, V_1, ...: a K load never queues behind the previous tile's V
+        for (int j = 0; j <= t.nkb && ok; ++j) {
+          if (j < t.nkb) {
+            const int st = gk % KVS;
+            if (!mbar_wait(smem_u32(&bar->k_empty[st]), ((gk / KVS) & 1) ^ 1, abort_flag, p.err,
+                           kErrWaitProducer)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = smem_u32(&bar->k_full[st]);
+            mbar_arrive_expect_tx(fb, L::KV_TILE);
+#pragma unroll
+            for (int c = 0; c < HD / 64; ++c)
+              tma_load_2d(sbase + L::OFF_K + st * L::KV_TILE + c * L::CHUNK, &tm, fb,
+                          kcol + c * 64, row0 + j * BN);
+            ++gk;
+          }
+          if (j >= 1) {
+            const int st = gv % KVS;
+            if (!mbar_wait(smem_u32(&bar->v_empty[st]), ((gv / KVS) & 1) ^ 1, abort_flag, p.err,
+                           kErrWaitProducer)) {
+              ok = false;
+              break;
+            }
+            const uint32_t fb = smem_u32(&bar->v_full[st]);
+            mbar_arrive_expect_tx(fb, L::KV_TILE);
+#pragma unroll
+            for (int c = 0; c < HD / 64; ++c)
+              tma_load_2d(sbase + L::OFF_V + st * L::KV_TILE + c * L::CHUNK, &tm, fb,
+                          vcol + c * 64, row0 + (j - 1) * BN);
+            ++gv;
+          }
+        }
+      }
+      tma_drain_ring(bar->k_full, KVS, gk);
+      tma_drain_ring(bar->v_full, KVS, gv);
+      tma_drain_ring(bar->q_full, QBUF, k);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      constexpr uint32_t IDESC_S = idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t IDESC_O = idesc_bf16_f32(BM, HD, false, true);
+      int k = 0, g = 0;  // items, key steps
+      bool ok = true;
+      for (; ok; ++k) {
+        const int qs = k % QBUF;
+        if (!mbar_wait(smem_u32(&bar->q_full[qs]), (k / QBUF) & 1, abort_flag, p.err, kErrWaitMma))
+          break;
+        const int id = item_slot[qs];
+        if (id < 0) break;
+        const Item t = decode_pp(id, p);
+        tc_fence_after();
+        // S_t(j) = Q_t K_j^T into tile t's S columns (K slot of step j already full)
+        auto issue_s = [&](int tt, int j) {
+          const int st = (g + j) % KVS;
+          const uint64_t qd = sdesc_sw128(sbase + L::OFF_Q + qs * L::Q_BYTES + tt * L::Q_TILE,
+                                          16, 1024);
+          const uint64_t kd = sdesc_sw128(sbase + L::OFF_K + st * L::KV_TILE, 16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const uint32_t off = ((kk >> 2) * L::CHUNK + (kk & 3) * 32) >> 4;
+            umma_bf16_ss(tmem + tt * BN, qd + off, kd + off, IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(&bar->s_full[tt]));
+        };
+        auto wait_k = [&](int j) -> bool {
+          const int gg = g + j;
+          if (!mbar_wait(smem_u32(&bar->k_full[gg % KVS]), (gg / KVS) & 1, abort_flag, p.err,
+                         kErrWaitMma))
+            return false;
+          tc_fence_after();
+          return true;
+        };
+        // O_t += P_t(j) V_j once tile t's softmax has written P_t(j)
+        auto issue_pv = [&](int tt, int j) -> bool {
+          const int gg = g + j, st = gg % KVS;
+          if (j == 0 && k > 0 &&
+              !mbar_wait(smem_u32(&bar->o_free[tt]), (k - 1) & 1, abort_flag, p.err, kErrWaitMma))
+            return false;
+          if (!mbar_wait(smem_u32(&bar->p_ready[tt]), gg & 1, abort_flag, p.err, kErrWaitMma))
+            return false;
+          tc_fence_after();
+          const uint64_t vd = sdesc_sw128(sbase + L::OFF_V + st * L::KV_TILE, L::CHUNK, 1024);
+          const uint32_t pa = tmem + tt * BN;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk)
+            umma_bf16_ts(tmem + kOCol + tt * HD, pa + kk * 8, vd + ((kk * 2048) >> 4), IDESC_O,
+                         (kk > 0 || j > 0) ? 1u : 0u);
+          return true;
+        };
+        ok = wait_k(0);
+        if (ok) {
+          issue_s(0, 0);
+          issue_s(1, 0);
+          umma_commit(smem_u32(&bar->k_empty[g % KVS]));
+        }
+        for (int j = 0; j < t.nkb && ok; ++j) {
+          const int gg = g + j;
+          if (!mbar_wait(smem_u32(&bar->v_full[gg % KVS]), (gg / KVS) & 1, abort_flag, p.err,
+                         kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          const bool more = j + 1 < t.nkb;
+          if (more && !wait_k(j + 1)) {
+            ok = false;
+            break;
+          }
+          if (!issue_pv(0, j)) {
+            ok = false;
+            break;
+          }
+          if (!more) umma_commit(smem_u32(&bar->o_done[0]));
+          if (more) issue_s(0, j + 1);
+          if (!issue_pv(1, j)) {
+            ok = false;
+            break;
+          }
+          umma_commit(smem_u32(&bar->v_empty[gg % KVS]));
+          if (more) {
+            issue_s(1, j + 1);
+            umma_commit(smem_u32(&bar->k_empty[(gg + 1) % KVS]));
+          } else {
+            umma_commit(smem_u32(&bar->o_done[1]));
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(&bar->q_empty[qs]));
+        g += t.nkb;
+      }
+      umma_commit(smem_u32(&bar->drain));
+      volatile int no_abort = 0;
+      mbar_wait(smem_u32(&bar->drain), 0, &no_abort, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue, warps 2-9
+    const int quad = warp & 3;
+    const int tt = (warp - 2) >> 2;  // tile: warps 2-5 -> A (head 2 hp), 6-9 -> B (2 hp + 1)
+    const int r = quad * 32 + lane;  // query row in the tile == TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t s_col = tt * BN, o_col = kOCol + tt * HD;
+    const float c = p.scale_log2;
+    int k = 0, g = 0;
+    bool ok = true;
+    for (; ok; ++k) {
+      const int qs = k % QBUF;
+      if (!mbar_wait(smem_u32(&bar->q_full[qs]), (k / QBUF) & 1, abort_flag, p.err, kErrWaitSoftmax))
+        break;
+      const int id = item_slot[qs];
+      if (id < 0) break;
+      const Item t = decode_pp(id, p);
+      const int q0 = t.qb * BM;
+      const int qpos = q0 + r;
+      float m_ref = -CUDART_INF_F;  // running reference max, log2 units
+      float l = 0.f;                // running row sum
+      for (int j = 0; j < t.nkb; ++j) {
+        const int gg = g + j;
+        if (!mbar_wait(smem_u32(&bar->s_full[tt]), gg & 1, abort_flag, p.err, kErrWaitSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float sv[BN];
+        {
+          uint32_t* su = reinterpret_cast<uint32_t*>(sv);
+#pragma unroll
+          for (int cc = 0; cc < BN / 32; ++cc) CFB_TMEM_LD32(lane_addr + s_col + cc * 32, (su + cc * 32));
+        }
+        tmem_ld_wait();
+        const int k0 = j * BN;
+        if ((k0 + BN - 1 > q0) || (k0 + BN > p.S)) {  // diagonal / ragged block: mask
+          const int lim = min(qpos, p.S - 1) - k0;  // keys with index <= lim are visible
+#pragma unroll
+          for (int i = 0; i < BN; ++i)
+            if (i > lim) sv[i] = -CUDART_INF_F;
+        }
+        float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
+#pragma unroll
+        for (int i = 0; i < BN; i += 8) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) m4[q] = fmax3f(m4[q], sv[i + 2 * q], sv[i + 2 * q + 1]);
+        }
+        const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * c;
+        const bool grow = (mx > m_ref + kRescaleThreshold) || (m_ref == -CUDART_INF_F);
+        float alpha = 1.f;
+        if (grow) {
+          const float m_new = fmaxf(m_ref, mx);
+          alpha = (m_ref == -CUDART_INF_F) ? 0.f : ex2_approx(m_ref - m_new);
+          m_ref = m_new;
+        }
+        const float nref = (m_ref == -CUDART_INF_F) ? 0.f : -m_ref;
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+        // P (bf16, two keys per column) over the first 64 of the tile's 128 S columns; the whole
+        // row of S is already in registers
+#pragma unroll
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float e0 = ex2_approx(fmaf(sv[cc * 32 + 2 * i], c, nref));
+            const float e1 = ex2_approx(fmaf(sv[cc * 32 + 2 * i + 1], c, nref));
+            rs[(2 * i) & 3] += e0;
+            rs[(2 * i + 1) & 3] += e1;
+            pk[i] = pack_bf16x2(e0, e1);
+          }
+          CFB_TMEM_ST16(lane_addr + s_col + cc * 16, pk);
+        }
+        l = l * alpha + ((rs[0] + rs[1]) + (rs[2] + rs[3]));
+        // a grown max rescales O (P V of step j-1 is complete: S of step j was issued after it)
+        if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int cc = 0; cc < HD / 32; ++cc) {
+            uint32_t o[32];
+            CFB_TMEM_LD32(lane_addr + o_col + cc * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            CFB_TMEM_ST32(lane_addr + o_col + cc * 32, o);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bar->p_ready[tt]));
+      }
+      if (!ok) break;
+      // epilogue: O / l and the LSE of this tile's head
+      if (!mbar_wait(smem_u32(&bar->o_done[tt]), k & 1, abort_flag, p.err, kErrWaitSoftmax)) break;
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int row0 = t.b * p.S, h = t.h + tt;
+      __nv_bfloat16* dst =
+          p.out + static_cast<long long>(row0 + min(qpos, p.S - 1)) * p.ld_out + h * HD;
+#pragma unroll
+      for (int cc = 0; cc < HD / 32; ++cc) {
+        uint32_t a[32];
+        CFB_TMEM_LD32(lane_addr + o_col + cc * 32, a);
+        tmem_ld_wait();
+        if (qpos < p.S) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + cc * 32);
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(a[8 * kq + 0]) * inv, __uint_as_float(a[8 * kq + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(a[8 * kq + 2]) * inv, __uint_as_float(a[8 * kq + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(a[8 * kq + 4]) * inv, __uint_as_float(a[8 * kq + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(a[8 * kq + 6]) * inv, __uint_as_float(a[8 * kq + 7]) * inv);
+            d4[kq] = u;
+          }
+        }
+      }
+      if (qpos < p.S)
+        p.lse[static_cast<long long>(row0 + qpos) * p.nh + h] = (m_ref + log2f(l)) * kLn2;
+      // O read: the next item's first P V of this tile may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar->o_free[tt]));
+      g += t.nkb;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (threadIdx.x == 0) {
+    // the last CTA to finish resets the work counter for the next launch
+    __threadfence();
+    if (atomicAdd(p.work + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(p.work, 0);
+      atomicExch(p.work + 1, 0);
+    }
+  }
+}
+
 int make_tmap_qkv(CUtensorMap* map, const void* qkv, long long rows, long long ld);
 
 template <int HD>
@@ -574,6 +983,24 @@ int launch(const void* qkv, long long ld, void* out, long long ld_out, float* ls
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+  }
+  // Two-tile kernel when head pairs share a K/V head (even GQA group); CFB_ATTN_PP=0 keeps the
+  // one-tile kernel.
+  static const bool pp_on = [] {
+    const char* e = std::getenv("CFB_ATTN_PP");
+    return !(e && e[0] == '0');
+  }();
+  if (pp_on && (nh / nkv) % 2 == 0) {
+    p.n_items = p.nqb * (nh / 2) * B;
+    auto kpp = attn_fwd_pp_kernel<HD>;
+    static bool configured_pp = false;
+    if (!configured_pp) {
+      cudaFuncSetAttribute(kpp, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemPP<HD>::BYTES);
+      configured_pp = true;
+    }
+    const int grid = p.n_items < n_sm ? p.n_items : n_sm;
+    kpp<<<grid, SmemPP<HD>::THREADS, SmemPP<HD>::BYTES, st>>>(tm, p);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
   }
   auto kern = attn_fwd_tc_kernel<HD>;
   static bool configured = false;
