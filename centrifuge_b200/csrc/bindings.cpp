@@ -748,6 +748,39 @@ void symm_pull_reduce(int64_t mc_base, int64_t peer_base_dev, int64_t W, int64_t
                "symm_pull_reduce");
 }
 
+void ex2_poly(const Tensor& x, Tensor& y) {
+  TORCH_CHECK(x.scalar_type() == at::kFloat && y.scalar_type() == at::kFloat &&
+                  x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel(),
+              "ex2_poly: contiguous fp32 tensors of equal size");
+  const c10::cuda::CUDAGuard guard(x.device());
+  CFB_CHECK_RC(cfb_ex2_poly(x.data_ptr<float>(), y.data_ptr<float>(), x.numel(), cur_stream()),
+               "ex2_poly");
+}
+
+// vocabulary-parallel cross entropy over symmetric per-row statistics (see cfb_ce_exchange)
+void ce_exchange(int64_t peer_stats_dev, int64_t P, const Tensor& labels, Tensor& loss,
+                 Tensor& lse, int64_t flags, int64_t ready_base, int64_t epoch,
+                 int64_t peer_flags_dev, int64_t done_off, int64_t me, Tensor& counter,
+                 Tensor& err) {
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels int64");
+  const int64_t T = labels.numel();
+  TORCH_CHECK(loss.scalar_type() == at::kFloat && lse.scalar_type() == at::kFloat &&
+                  loss.numel() == T && lse.numel() == T,
+              "loss / lse fp32 [T]");
+  TORCH_CHECK(counter.scalar_type() == at::kInt && counter.numel() >= 1, "counter");
+  check_status(err, "ce_exchange");
+  const c10::cuda::CUDAGuard guard(labels.device());
+  CFB_CHECK_RC(cfb_ce_exchange(reinterpret_cast<const float* const*>(peer_stats_dev), P, T,
+                               reinterpret_cast<const long long*>(labels.data_ptr<int64_t>()),
+                               loss.data_ptr<float>(), lse.data_ptr<float>(),
+                               reinterpret_cast<const uint32_t*>(flags), ready_base,
+                               static_cast<uint32_t>(epoch),
+                               reinterpret_cast<uint32_t* const*>(peer_flags_dev), done_off, me,
+                               reinterpret_cast<uint32_t*>(counter.data_ptr<int>()),
+                               err.data_ptr<int>(), cur_stream()),
+               "ce_exchange");
+}
+
 // buf = 0 unless err[0] != 0 (a failed peer wait: a peer may still be reading buf)
 void zero_unless_error(Tensor& buf, const Tensor& err) {
   TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous(),
@@ -830,6 +863,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("gather_rows", &gather_rows);
   m.def("embedding_fwd", &embedding_fwd);
+  m.def("ce_exchange", &ce_exchange);
+  m.def("ex2_poly", &ex2_poly);
   m.def("embedding_bwd", &embedding_bwd, py::arg("dy"), py::arg("ids"), py::arg("id_rows"),
         py::arg("dtable"), py::arg("deterministic") = true);
   m.def("ce_fwd", &ce_fwd);

@@ -130,6 +130,51 @@ __global__ void __launch_bounds__(512) zero_unless_error_kernel(float* __restric
     buf[i] = 0.f;
 }
 
+// Vocabulary-parallel cross entropy: every rank of the tensor-parallel group holds, per row,
+// (max, sum of exp(logit - max), label logit or 0) of its vocabulary shard in a symmetric
+// buffer [3][T] (stats_q of rank q through peer_stats[q]).  Each block waits (bounded) until
+// every rank has raised ready[q] >= epoch, then one thread per row combines the P triples:
+//   M = max_q m_q,  Z = sum_q s_q exp(m_q - M),  lse = M + log Z,  loss = lse - sum_q t_q
+// (loss 0 for labels < 0).  The last block to finish tells every rank that this rank has read
+// their buffers (done[me] = epoch), after which they may be rewritten.  After a failed wait
+// nothing is read and the rows keep loss 0.
+__global__ void __launch_bounds__(256) ce_exchange_kernel(
+    const float* const* peer_stats, int P, int T, const long long* __restrict__ labels,
+    float* __restrict__ loss, float* __restrict__ lse, const uint32_t* flags, int ready_base,
+    uint32_t epoch, uint32_t* const* peer_flags, int done_off, int me, uint32_t* counter,
+    int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = wait_flags(flags, ready_base, 1, P, epoch, err, kErrPeerWait) ? 1 : 0;
+  __syncthreads();
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row < T) {
+    float l = 0.f, z = 0.f;
+    if (ok) {
+      float M = -INFINITY;
+      for (int q = 0; q < P; ++q) M = fmaxf(M, peer_stats[q][row]);
+      float tgt = 0.f;
+      for (int q = 0; q < P; ++q) {
+        const float* st = peer_stats[q];
+        z += st[T + row] * __expf(st[row] - M);
+        tgt += st[2 * T + row];
+      }
+      z = M + __logf(z);
+      l = labels[row] >= 0 ? z - tgt : 0.f;
+    }
+    loss[row] = l;
+    lse[row] = z;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(counter, 1u) == gridDim.x - 1u) {
+      atomicExch(counter, 0u);
+      if (ok)
+        for (int q = 0; q < P; ++q) st_release_sys(peer_flags[q] + done_off + me, epoch);
+    }
+  }
+}
+
 }  // namespace comm
 }  // namespace cfb
 
@@ -158,6 +203,18 @@ int cfb_symm_pull_reduce(const float* mc_base, const float* const* peer_base_dev
   if (blocks > 148 * 4) blocks = 148 * 4;
   pull_reduce_kernel<<<static_cast<int>(blocks), 512, 0, st>>>(
       mc_base, peer_base_dev, W, off, n, dst, scale, flags, bucket, epoch, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int cfb_ce_exchange(const float* const* peer_stats, int P, int T, const long long* labels,
+                    float* loss, float* lse, const uint32_t* flags, int ready_base,
+                    uint32_t epoch, uint32_t* const* peer_flags, int done_off, int me,
+                    uint32_t* counter, int* err, cudaStream_t st) {
+  if (P <= 0 || P > 1024 || T < 0) return -11;
+  if (T == 0) return 0;
+  ce_exchange_kernel<<<(T + 255) / 256, 256, 0, st>>>(peer_stats, P, T, labels, loss, lse, flags,
+                                                     ready_base, epoch, peer_flags, done_off, me,
+                                                     counter, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

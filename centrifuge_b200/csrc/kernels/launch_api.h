@@ -204,6 +204,16 @@ int cfb_ce_combine(const float* pmax, const float* psum, const float* ptgt, int 
 // NVLink peer-memory gradient reduction (comm_sm100.cu).
 int cfb_symm_signal(uint32_t* const* peer_flags_dev, int W, int off, uint32_t epoch,
                     cudaStream_t st);
+// Vocabulary-parallel cross entropy: combine the P ranks' per-row (max, sum exp, label logit)
+// statistics (symmetric buffers [3][T], peer_stats device array [P]) into loss / lse after a
+// bounded wait on ready[ready_base + q] >= epoch; then raise done[done_off + me] = epoch at every
+// rank.  `counter` is a device word, zero at rest.
+int cfb_ce_exchange(const float* const* peer_stats, int P, int T, const long long* labels,
+                    float* loss, float* lse, const uint32_t* flags, int ready_base,
+                    uint32_t epoch, uint32_t* const* peer_flags, int done_off, int me,
+                    uint32_t* counter, int* err, cudaStream_t st);
+// The attention forward's software base-2 exponential, element-wise (accuracy tests).
+int cfb_ex2_poly(const float* x, float* y, int n, cudaStream_t st);
 int cfb_symm_wait(const uint32_t* flags, int base, int stride, int n, uint32_t epoch, int* err,
                   cudaStream_t st);
 int cfb_symm_pull_reduce(const float* mc_base, const float* const* peer_base_dev, int W,

@@ -117,6 +117,7 @@ class TPLlamaCore(torch.nn.Module):
         self.comm_sets = 1
         self._fwd_count = 0
         self._comm = None
+        self._ce_x = None  # vocabulary-parallel loss exchange over NVLink (fused mode)
 
     def reduce_replicated_grads(self) -> None:
         """Sum the gradients of replicated weights (embedding, RMSNorm) over the TP group.
@@ -197,7 +198,13 @@ class TPLlamaCore(torch.nn.Module):
         else:
             lab = labels.to(torch.long).clone()
         lab = lab.reshape(-1).contiguous()
-        if P > 1:
+        if P > 1 and self.use_fused_comm and logits.is_cuda:
+            # row statistics exchanged over NVLink by one kernel (parallel/tp_fused.py)
+            if self._ce_x is None or self._ce_x.T < lab.numel():
+                from ..parallel.tp_fused import VocabParallelCE
+                self._ce_x = VocabParallelCE(tp, lab.numel(), x.device)
+            loss, lse_ce = self._ce_x(logits, lab, self.vocab_start)
+        elif P > 1:
             pmax, psum, ptgt = fused.ce_partial(logits, lab, self.vocab_start)
             gmax = tp.all_reduce_(pmax.clone(), torch.distributed.ReduceOp.MAX)
             tot = tp.all_reduce_(psum * torch.exp(pmax - gmax))

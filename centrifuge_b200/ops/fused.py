@@ -169,11 +169,12 @@ def ce_bwd(logits: torch.Tensor, labels: torch.Tensor, lse: torch.Tensor, dloss:
     return out
 
 
-def ce_partial(logits: torch.Tensor, labels: torch.Tensor, vocab_start: int):
-    """Per-row (max, sum exp(logit - max), label logit or 0) of one vocabulary shard."""
+def ce_partial(logits: torch.Tensor, labels: torch.Tensor, vocab_start: int, out=None):
+    """Per-row (max, sum exp(logit - max), label logit or 0) of one vocabulary shard;
+    ``out``: three fp32 ``[rows]`` tensors to write them into."""
     rows = logits.shape[0]
     f32 = dict(dtype=torch.float32, device=logits.device)
-    pmax, psum, ptgt = (torch.empty(rows, **f32) for _ in range(3))
+    pmax, psum, ptgt = out if out is not None else (torch.empty(rows, **f32) for _ in range(3))
     if not logits.is_cuda:
         lf = logits.float()
         pmax.copy_(lf.max(-1).values)

@@ -173,6 +173,60 @@ class TPFusedComm:
         return out
 
 
+class VocabParallelCE:
+    """Vocabulary-parallel cross entropy with the row statistics exchanged over NVLink.
+
+    Replaces the three all-reduces (max, rescaled sum of exp, label logit) of the Megatron
+    vocabulary-parallel loss (reference model/megatronlm.py:256-263): every rank writes its
+    shard's per-row (max, sum exp, label logit) into its copy of a symmetric buffer (two slots,
+    alternating by call), raises a ready flag at every rank, and one kernel per rank combines
+    the P triples of each row into lse and loss after a bounded wait
+    (``cfb_ce_exchange``).  A slot is rewritten two calls later, once every rank has reported
+    (done flag) that it read it.  Every rank of the group makes the same sequence of calls."""
+
+    def __init__(self, tp, T: int, device):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from ..ops._ext import status_block
+        self.tp, self.P, self.rank, self.T = tp, tp.size, tp.rank, T
+        self.device = torch.device(device)
+        self.stats = symm_mem.empty(2 * 3 * T, dtype=torch.float32, device=self.device)
+        self.shdl = symm_mem.rendezvous(self.stats, tp.group)
+        self.flags = symm_mem.empty(2 * self.P, dtype=torch.int32, device=self.device)
+        self.flags.zero_()
+        self.fhdl = symm_mem.rendezvous(self.flags, tp.group)
+        self.peer_flags_dev = int(self.fhdl.buffer_ptrs_dev)
+        sb = [int(x) for x in self.shdl.buffer_ptrs]
+        self.peers = [torch.tensor([b + i * 3 * T * 4 for b in sb], dtype=torch.int64,
+                                   device=self.device) for i in range(2)]
+        self.counter = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.err = status_block(self.device)
+        self.epoch = 0
+        torch.cuda.synchronize(self.device)
+        dist.barrier(tp.group)
+
+    def __call__(self, logits: torch.Tensor, labels: torch.Tensor, vocab_start: int):
+        """``logits`` [T, V/P] bf16 of this rank's shard, ``labels`` [T] (global ids, < 0
+        ignored); returns (loss [T], lse [T]) fp32, the same on every rank."""
+        T, P = labels.numel(), self.P
+        assert T <= self.T and labels.dtype == torch.long
+        k = kernels()
+        self.epoch += 1
+        e, i = self.epoch, self.epoch & 1
+        if e > 2:  # every rank has read this slot's previous contents
+            k.symm_wait(self.flags.data_ptr(), P, 1, P, e - 2, self.err)
+        st = self.stats[i * 3 * self.T:i * 3 * self.T + 3 * T].view(3, T)
+        fused.ce_partial(logits, labels, vocab_start, out=(st[0], st[1], st[2]))
+        # the exchange kernel indexes a slot as [3][T] of this call's T: offsets use T
+        k.symm_signal(self.peer_flags_dev, P, self.rank, e)
+        loss = torch.empty(T, dtype=torch.float32, device=self.device)
+        lse = torch.empty_like(loss)
+        k.ce_exchange(self.peers[i].data_ptr(), P, labels, loss, lse, self.flags.data_ptr(), 0,
+                      e, self.peer_flags_dev, P, self.rank, self.counter, self.err)
+        return loss, lse
+
+
 class Segments:
     """Per-rank row segments of a sequence-parallel tensor: rank q owns rows
     ``[start[q], start[q] + counts[q])`` (host lists) and ``dev`` is the int32 device prefix

@@ -238,3 +238,60 @@ def test_tp2_pp2_fused_collectives_match_nccl():
         for dl, dg in rows:
             assert dl < 1e-2, (rank, kind, rows)
             assert dg < 3e-2, (rank, kind, rows)
+
+
+def _ce_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from centrifuge_b200.ops import kernels
+        from centrifuge_b200.parallel.tensor_parallel import TPGroup
+        from centrifuge_b200.parallel.tp_fused import VocabParallelCE
+        tp = TPGroup(dist.group.WORLD)
+        V = 1000 * world
+        x = VocabParallelCE(tp, 512, "cuda")
+        errs = []
+        for call, T in enumerate((512, 300, 512, 77)):  # slots alternate, rows vary
+            g = torch.Generator(device="cuda").manual_seed(100 + call)
+            logits = (4 * torch.randn(T, V, generator=g, device="cuda")).bfloat16()
+            labels = torch.randint(0, V, (T,), generator=g, device="cuda")
+            labels[::7] = -100
+            shard = logits[:, rank * 1000:(rank + 1) * 1000].contiguous()
+            loss, lse = x(shard, labels, rank * 1000)
+            lf = logits.float()
+            want_lse = torch.logsumexp(lf, -1)
+            want = torch.nn.functional.cross_entropy(lf, labels.clamp(min=0), reduction="none")
+            want = torch.where(labels >= 0, want, torch.zeros_like(want))
+            torch.cuda.synchronize()
+            errs.append(max(float((loss - want).abs().max()), float((lse - want_lse).abs().max())))
+        q.put((rank, errs, kernels().gemm_error_word(rank, True)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_vocab_parallel_ce_exchange():
+    """Vocabulary-parallel cross entropy with the row statistics exchanged over NVLink equals the
+    fp32 cross entropy of the full logits, over calls that alternate the buffer slots."""
+    import torch.multiprocessing as mp
+
+    from tests.dist_utils import free_port
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_ce_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    outs = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, errs, err_word in outs:
+        assert err_word == 0, (rank, err_word)
+        assert max(errs) < 2e-3, (rank, errs)
