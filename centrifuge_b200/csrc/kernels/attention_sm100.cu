@@ -105,6 +105,24 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Software base-2 exponential on the FMA pipe, for a share of the scores while the MUFU unit
+// is the busiest pipe.  Cody-Waite style range reduction x = j + f with j = round(x) (the
+// 1.5 * 2^23 rounding constant) and f in [-1/2, 1/2], a degree-3 polynomial for 2^f fitted
+// here by the Remez exchange algorithm on the relative error (max relative error 7.5e-5, far
+// below the bf16 rounding of P), and 2^j added into the exponent field.  Inputs below -125
+// are clamped (result about 2^-125 instead of 0; masked scores are -inf).
+__device__ __forceinline__ float ex2_poly(float x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x = fmaxf(x, -125.0f);
+  const float t = x + kRound;
+  const float f = x - (t - kRound);
+  float p = fmaf(0.0551716685295105f, f, 0.2426111251115799f);
+  p = fmaf(p, f, 0.6932609677314758f);
+  p = fmaf(p, f, 0.9999280571937561f);
+  const int j = __float_as_int(t) - __float_as_int(kRound);
+  return __int_as_float(__float_as_int(p) + (j << 23));
+}
+
 // Three-input maximum (sm_100).
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float y;
@@ -599,7 +617,8 @@ __device__ __forceinline__ Item decode_pp(int id, const Params& p) {
   return t;
 }
 
-template <int HD>
+// PE: every PE-th pair of scores takes the software exponential (0: all on MUFU)
+template <int HD, int PE = 0>
 __global__ void __launch_bounds__(SmemPP<HD>::THREADS, 1)
     attn_fwd_pp_kernel(const __grid_constant__ CUtensorMap tm, const Params p) {
   using L = SmemPP<HD>;
@@ -879,8 +898,11 @@ __global__ void __launch_bounds__(SmemPP<HD>::THREADS, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float e0 = ex2_approx(fmaf(sv[cc * 32 + 2 * i], c, nref));
-            const float e1 = ex2_approx(fmaf(sv[cc * 32 + 2 * i + 1], c, nref));
+            const float x0 = fmaf(sv[cc * 32 + 2 * i], c, nref);
+            const float x1 = fmaf(sv[cc * 32 + 2 * i + 1], c, nref);
+            const bool soft = PE > 0 && (i % (PE > 0 ? PE : 1)) == (PE > 0 ? PE : 1) - 1;
+            const float e0 = soft ? ex2_poly(x0) : ex2_approx(x0);
+            const float e1 = soft ? ex2_poly(x1) : ex2_approx(x1);
             rs[(2 * i) & 3] += e0;
             rs[(2 * i + 1) & 3] += e1;
             pk[i] = pack_bf16x2(e0, e1);
@@ -955,6 +977,12 @@ __global__ void __launch_bounds__(SmemPP<HD>::THREADS, 1)
   }
 }
 
+// y[i] = ex2_poly(x[i]): the software exponential on its own, for accuracy tests
+__global__ void ex2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = ex2_poly(x[i]);
+}
+
 int make_tmap_qkv(CUtensorMap* map, const void* qkv, long long rows, long long ld);
 
 template <int HD>
@@ -990,13 +1018,20 @@ int launch(const void* qkv, long long ld, void* out, long long ld_out, float* ls
     const char* e = std::getenv("CFB_ATTN_PP");
     return !(e && e[0] == '0');
   }();
+  // CFB_ATTN_POLY=n (4 or 8): every n-th pair of scores uses the FMA-pipe exponential
+  static const int poly = [] {
+    const char* e = std::getenv("CFB_ATTN_POLY");
+    return e ? std::atoi(e) : 0;
+  }();
   if (pp_on && (nh / nkv) % 2 == 0) {
     p.n_items = p.nqb * (nh / 2) * B;
-    auto kpp = attn_fwd_pp_kernel<HD>;
-    static bool configured_pp = false;
-    if (!configured_pp) {
+    auto kpp = poly == 4 ? attn_fwd_pp_kernel<HD, 4>
+             : poly == 8 ? attn_fwd_pp_kernel<HD, 8> : attn_fwd_pp_kernel<HD, 0>;
+    static bool configured_pp[3] = {false, false, false};
+    const int pi = poly == 4 ? 1 : poly == 8 ? 2 : 0;
+    if (!configured_pp[pi]) {
       cudaFuncSetAttribute(kpp, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemPP<HD>::BYTES);
-      configured_pp = true;
+      configured_pp[pi] = true;
     }
     const int grid = p.n_items < n_sm ? p.n_items : n_sm;
     kpp<<<grid, SmemPP<HD>::THREADS, SmemPP<HD>::BYTES, st>>>(tm, p);
@@ -1036,4 +1071,10 @@ int cfb_attn_fwd_tc(const void* qkv, long long ld_qkv, void* out, long long ld_o
     return cfb::attn_tc::launch<128>(qkv, ld_qkv, out, ld_out, lse, B, S, nh, nkv, scale, work,
                                      err, st);
   return -12;
+}
+
+int cfb_ex2_poly(const float* x, float* y, int n, cudaStream_t st) {
+  if (n <= 0) return n == 0 ? 0 : -11;
+  cfb::attn_tc::ex2_poly_kernel<<<(n + 255) / 256, 256, 0, st>>>(x, y, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -198,6 +198,26 @@ def test_embedding_bwd_deterministic():
     fused.embedding_bwd(dy, ids[:R], dt)
     assert rel_err(dt, base.clone().index_add_(0, ids[:R], dy.float())) < 1e-6
 
+
+def test_ex2_poly_accuracy():
+    """The attention forward's FMA-pipe exponential: relative error within 1e-4 of 2^x over the
+    range the softmax uses ([-125, 8]), exactly the powers of two at integers, 2^-125 at most
+    for masked (-inf) scores."""
+    from centrifuge_b200.ops import kernels
+    x = torch.cat([torch.linspace(-125.0, 8.0, 1 << 20, device=dev),
+                   torch.arange(-30, 9, device=dev, dtype=torch.float32)])
+    y = torch.empty_like(x)
+    kernels().ex2_poly(x, y)
+    want = torch.exp2(x.double())
+    rel = ((y.double() - want).abs() / want).max().item()
+    assert rel < 1e-4, rel
+    # MUFU ex2.approx is specified to about 2 ulp; the polynomial's 7.5e-5 is far below the
+    # bf16 rounding (2^-9) that P goes through
+    z = torch.tensor([-float("inf"), -1000.0], device=dev)
+    w = torch.empty_like(z)
+    kernels().ex2_poly(z, w)
+    assert (w >= 0).all() and (w <= 2.0 ** -124).all()
+
 def test_cross_entropy():
     torch.manual_seed(6)
     T, V = 64, 32000
