@@ -90,6 +90,9 @@ def main():
         for _ in range(a.warmup):
             step()
         torch.cuda.synchronize()
+        if a.pp > 1:
+            tr.timing = True
+            tr.busy_ms()
         dist.barrier()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
@@ -101,6 +104,19 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t) / a.steps
         tokens = M * a.mbs * a.seq
+        pipe = {}
+        if a.pp > 1:
+            # bubble of this stage = 1 - (its compute time / step time); 1F1B theory for equal
+            # stages: (pp - 1) / (M + pp - 1)
+            busy = tr.busy_ms() / a.steps
+            tr.timing = False
+            b = torch.tensor([1.0 - busy / ms, busy], device=dev)
+            bmax, bmin = b.clone(), b.clone()
+            dist.all_reduce(bmax, op=dist.ReduceOp.MAX)
+            dist.all_reduce(bmin, op=dist.ReduceOp.MIN)
+            pipe = {"bubble_fraction_max": float(bmax[0]), "bubble_fraction_min": float(bmin[0]),
+                    "stage_busy_ms_max": float(bmax[1]), "stage_busy_ms_min": float(bmin[1]),
+                    "bubble_1f1b_theory": (a.pp - 1) / (M + a.pp - 1)}
         if rank == 0:
             print(json.dumps({
                 "metric": "train tokens/sec (device-timed, max over ranks)",
@@ -111,6 +127,7 @@ def main():
                            "global_batch": M * a.mbs,
                            "parallelism": f"tp{a.tp}" + (f"pp{a.pp}-1f1b" if a.pp > 1 else "-sp")},
                 "comm": (core._comm.kind if core._comm is not None else "nccl"),
+                **({"pipeline": pipe} if pipe else {}),
                 "dtype": "bf16", "data": "synthetic"}), flush=True)
     dist.barrier()
     dist.destroy_process_group()

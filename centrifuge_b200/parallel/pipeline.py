@@ -74,6 +74,10 @@ class PipelineTrainer:
         self.device = core.device
         self._sends: List = []
         self._pending = {}  # posted receives: (kind, micro-batch) -> (work, tensor)
+        # timing=True: CUDA events around every forward / backward compute of this stage
+        # (after its receive, before its send), read by busy_ms() to measure the bubble
+        self.timing = False
+        self._events: List = []
         # device errors (bounded waits that ran out, bad masks) surface one step late
         self.status = None
         if check_device_errors and torch.device(self.device).type == "cuda":
@@ -105,6 +109,24 @@ class PipelineTrainer:
         B, S = batch[0].shape
         return (B * S // self.g.tp, self.core.cfg.hidden_size)
 
+    def _mark(self, start=None):
+        """Record a CUDA event (``timing`` only); with ``start``, close the interval."""
+        if not self.timing or torch.device(self.device).type != "cuda":
+            return None
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        if start is not None:
+            self._events.append((start, ev))
+        return ev
+
+    def busy_ms(self) -> float:
+        """Device time spent in this stage's forward / backward compute since the last call
+        (synchronises); the rest of a step is the pipeline bubble and communication waits."""
+        torch.cuda.synchronize(self.device)
+        t = sum(a.elapsed_time(b) for a, b in self._events)
+        self._events.clear()
+        return t
+
     def _drain_sends(self) -> None:
         for w, _ in self._sends:
             w.wait()
@@ -120,8 +142,10 @@ class PipelineTrainer:
             hidden = self._take(("f", i), self._fwd_shape(batches[i]), dt, self.g.prev)
             if i + 1 < len(batches):
                 self._post(("f", i + 1), self._fwd_shape(batches[i + 1]), dt, self.g.prev)
+        t0 = self._mark()
         out = self.core(input_ids=ids, hidden=hidden, batch_shape=(B, S))
         if not self.last:
+            self._mark(t0)
             self._isend(out.hidden.detach(), self.g.next)
             if prefetch_bwd >= 0:
                 pb, ps = batches[prefetch_bwd][0].shape
@@ -136,16 +160,19 @@ class PipelineTrainer:
         else:
             loss = token_filter_loss(ids, None, mask, None, None, None, True,
                                      per_token_loss=out.token_loss)
+        self._mark(t0)
         return {"i": i, "ids": ids, "loss": loss, "mask": mask, "B": B, "S": S}
 
     def _backward(self, st):
         B, S = st["B"], st["S"]
         H = self.core.cfg.hidden_size
         if self.last:
+            t0 = self._mark()
             self.core.pending_input_grad = None
             st["loss"].backward()
             dx = self.core.pending_input_grad
             mask = st["mask"]
+            self._mark(t0)
         else:
             mask = self._take(("m", st["i"]), (B, S), torch.long, self.g.next)
             filtered = bool(self.drop_rate > 0)
@@ -158,7 +185,9 @@ class PipelineTrainer:
             grad = self._take(("g", st["i"]), (lay.C, H), self.core.flat.data.dtype, self.g.next)
             fn = st["out"].hidden.grad_fn
             sv = fn.saved if fn is not None else None
+            t0 = self._mark()
             dx = self.core._backward_impl(sv, grad, state)
+            self._mark(t0)
             if fn is not None:
                 fn.saved = None
         if not self.first:
