@@ -32,6 +32,12 @@ def main():
     ap.add_argument("--mbs", type=int, default=4)
     ap.add_argument("--global_batch", type=int, default=32)
     ap.add_argument("--micro", type=int, default=None, help="pipeline micro-batches")
+    ap.add_argument("--head-cost", type=float, default=None,
+                    help="LM head + loss cost in decoder layers for the stage split (default: "
+                         "FLOP estimate; stage busy times at Llama-3-8B TP2 S4096 measured ~5)")
+    ap.add_argument("--even-stages", action="store_true",
+                    help="split layers evenly over pipeline stages (default: balance the LM "
+                         "head's cost)")
     ap.add_argument("--drop", type=float, nargs="+", default=[0.5])
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
@@ -50,7 +56,8 @@ def main():
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     from centrifuge_b200.config import get_model_config
     from centrifuge_b200.models.tp_llama import TPLlamaCore
-    from centrifuge_b200.parallel.pipeline import PipelineTrainer, build_groups, stage_layers
+    from centrifuge_b200.parallel.pipeline import (PipelineTrainer, build_groups,
+                                                   head_cost_layers, stage_layers)
     from centrifuge_b200.parallel.zero import ZeroAdamW
     from centrifuge_b200.trainer import Trainer
     from centrifuge_b200.data.synthetic import SyntheticTokenData
@@ -61,7 +68,10 @@ def main():
     cfg.max_position_embeddings = max(cfg.max_position_embeddings, a.seq)
     dev = torch.device("cuda", local)
     g = build_groups(a.tp, a.pp)
-    layers = stage_layers(cfg.num_hidden_layers, a.pp, g.stage)
+    # stages balanced by cost (the last one also runs the LM head) unless --even-stages
+    hc = 0.0 if a.even_stages else (a.head_cost if a.head_cost is not None
+                                    else head_cost_layers(cfg, a.seq))
+    layers = stage_layers(cfg.num_hidden_layers, a.pp, g.stage, head_cost=hc)
     core = TPLlamaCore(cfg, g.tp_group, device=dev, first=layers.start, last=layers.stop,
                        has_embed=g.stage == 0, has_head=g.stage == a.pp - 1)
     core.use_fused_comm = a.comm == "fused" and a.tp > 1
@@ -123,6 +133,8 @@ def main():
                 "value": tokens / (ms / 1000), "unit": "tokens/s", "n_gpus": world,
                 "ms_per_step": ms, "steps": a.steps, "warmup": a.warmup, "drop_rate": drop,
                 "config": {"model": cfg.name, "layers": cfg.num_hidden_layers, "seq_len": a.seq,
+                           "stage0_layers": len(stage_layers(cfg.num_hidden_layers, a.pp, 0,
+                                                             head_cost=hc)),
                            "micro_batch": a.mbs, "micro_batches": M,
                            "global_batch": M * a.mbs,
                            "parallelism": f"tp{a.tp}" + (f"pp{a.pp}-1f1b" if a.pp > 1 else "-sp")},

@@ -30,10 +30,50 @@ from ..loss import keep_count, token_filter_loss
 from .tensor_parallel import KeptLayout
 
 
-def stage_layers(num_layers: int, pp: int, stage: int) -> range:
-    per, rem = divmod(num_layers, pp)
-    start = stage * per + min(stage, rem)
-    return range(start, start + per + (1 if stage < rem else 0))
+def stage_layers(num_layers: int, pp: int, stage: int, head_cost: float = 0.0,
+                 embed_cost: float = 0.0) -> range:
+    """Layer range of pipeline stage ``stage``.
+
+    Without costs: the even split of the reference's stage demo (``per + (stage < rem)``
+    layers).  With ``head_cost`` / ``embed_cost`` (the LM head on the last stage and the
+    embedding on the first, in units of one decoder layer): contiguous ranges that minimise the
+    largest stage cost, every stage keeping at least one layer, so that the stage with the head
+    does not set the pipeline's pace alone."""
+    if head_cost <= 0.0 and embed_cost <= 0.0:
+        per, rem = divmod(num_layers, pp)
+        start = stage * per + min(stage, rem)
+        return range(start, start + per + (1 if stage < rem else 0))
+    assert num_layers >= pp, "every stage needs a layer"
+    INF = float("inf")
+
+    def cost(s, a, b):
+        return (b - a) + (embed_cost if s == 0 else 0.0) + (head_cost if s == pp - 1 else 0.0)
+
+    # best[s][i]: smallest possible max stage cost when stages 0..s-1 cover layers [0, i)
+    best = [[INF] * (num_layers + 1) for _ in range(pp + 1)]
+    cut = [[0] * (num_layers + 1) for _ in range(pp + 1)]
+    best[0][0] = 0.0
+    for s_ in range(1, pp + 1):
+        for i in range(s_, num_layers - (pp - s_) + 1):
+            for j in range(s_ - 1, i):
+                v = max(best[s_ - 1][j], cost(s_ - 1, j, i))
+                if v < best[s_][i] - 1e-12:
+                    best[s_][i], cut[s_][i] = v, j
+    bounds = [num_layers]
+    for s_ in range(pp, 0, -1):
+        bounds.append(cut[s_][bounds[-1]])
+    bounds = bounds[::-1]  # [0, b1, ..., num_layers]
+    return range(bounds[stage], bounds[stage + 1])
+
+
+def head_cost_layers(cfg, seq_len: int) -> float:
+    """FLOPs of the LM head (and its loss) per token in units of one decoder layer's FLOPs
+    (projections plus causal attention at ``seq_len``)."""
+    H, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
+    hd = getattr(cfg, "head_dim", None) or H // cfg.num_attention_heads
+    q, kv = cfg.num_attention_heads * hd, cfg.num_key_value_heads * hd
+    layer = H * (q + 2 * kv) + q * H + 3 * H * F + q * seq_len  # causal attention ~ 2 S q / 2
+    return V * H / layer
 
 
 @dataclass

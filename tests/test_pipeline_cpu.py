@@ -70,3 +70,18 @@ def test_tp2_pp2_matches_single(drop, tmp_path):
             v = torch.from_numpy(v)
             err = ((v - wp[name]).norm() / (wp[name].norm() + 1e-12)).item()
             assert err < 1e-4, (r["stage"], name, err)
+
+
+def test_stage_split_balances_head_cost():
+    from centrifuge_b200.parallel.pipeline import stage_layers
+    # even split without costs (reference stage demo)
+    assert [len(stage_layers(22, 4, s)) for s in range(4)] == [6, 6, 5, 5]
+    # the last stage also runs the LM head: it gets fewer layers, contiguous and complete
+    for L, pp, hc in ((32, 2, 2.2), (32, 4, 5.0), (8, 2, 5.0), (5, 5, 3.0)):
+        rs = [stage_layers(L, pp, s, head_cost=hc) for s in range(pp)]
+        assert rs[0].start == 0 and rs[-1].stop == L
+        assert all(a.stop == b.start and len(a) >= 1 for a, b in zip(rs, rs[1:]))
+        costs = [len(r) + (hc if s == pp - 1 else 0.0) for s, r in enumerate(rs)]
+        even = [len(stage_layers(L, pp, s)) + (hc if s == pp - 1 else 0.0) for s in range(pp)]
+        assert max(costs) <= max(even)
+    assert [len(stage_layers(32, 2, s, head_cost=2.2)) for s in range(2)] == [17, 15]
