@@ -26,14 +26,16 @@
 // items by ascending key block, then dQ items by descending query block).  The A/B tiles of an
 // item (K,V or Q,dO) are double-buffered so the next item's tiles load while the current one
 // finishes, and an item's epilogue (TMEM -> global) overlaps the next item's first score tiles.
-// Roles: warp 0 TMA + scheduling, warp 1 MMA issue (one thread), warps 2-9 softmax/epilogue
-// (two warps per TMEM lane quadrant, each taking half of the 64 columns).  Every barrier phase is
+// Roles: warp 0 TMA + scheduling, warp 1 MMA issue (one thread), NSW = 8 (or 16) softmax /
+// epilogue warps: NSW / 4 warps per TMEM lane quadrant, each taking 64 / (NSW / 4) of the 64
+// columns.  Every barrier phase is
 // derived from running counters (items taken, score tiles processed) that all roles advance
 // identically.  All waits are bounded (sm100_common.cuh).
 #include "sm100_common.cuh"
 #include "launch_api.h"
 
 #include <math_constants.h>
+#include <cstdlib>
 
 namespace cfb {
 namespace attn_bwd_tc {
@@ -131,22 +133,38 @@ __device__ __forceinline__ Item decode(int id, const Params& p) {
   return t;
 }
 
-// Thread's 32 columns of a 64-column bf16 row tile in 128B-swizzled K-major layout.
-__device__ __forceinline__ void write_row_half(uint32_t tile, int r, int half, const uint32_t* pk) {
+// Thread's CPT columns (part `part` of the row) of a 64-column bf16 row tile in 128B-swizzled
+// K-major layout: CPT / 8 pieces of 16 bytes.
+template <int CPT>
+__device__ __forceinline__ void write_row_part(uint32_t tile, int r, int part, const uint32_t* pk) {
   const uint32_t rowbase = tile + r * 128;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int piece = half * 4 + i;
+  for (int i = 0; i < CPT / 8; ++i) {
+    const int piece = part * (CPT / 8) + i;
     st_shared_v4(rowbase + ((piece ^ (r & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2],
                  pk[4 * i + 3]);
   }
 }
 
-// Store 32 fp32 TMEM columns as bf16 (times `mul`) to 64 contiguous bytes of global memory.
-__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t* v, float mul) {
+// Load N (8, 16 or 32) consecutive TMEM columns of the thread's lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld_n(uint32_t taddr, uint32_t* r) {
+  if constexpr (N == 32) {
+    CFB_TMEM_LD32(taddr, r);
+  } else if constexpr (N == 16) {
+    CFB_TMEM_LD16(taddr, r);
+  } else {
+    static_assert(N == 8, "TMEM load width");
+    CFB_TMEM_LD8(taddr, r);
+  }
+}
+
+// Store N (a multiple of 8) fp32 TMEM columns as bf16 (times `mul`) to 2 N contiguous bytes.
+template <int N>
+__device__ __forceinline__ void store_row_n(__nv_bfloat16* dst, const uint32_t* v, float mul) {
   uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < N / 8; ++k) {
     uint4 a;
     a.x = pack_bf16x2(__uint_as_float(v[8 * k + 0]) * mul, __uint_as_float(v[8 * k + 1]) * mul);
     a.y = pack_bf16x2(__uint_as_float(v[8 * k + 2]) * mul, __uint_as_float(v[8 * k + 3]) * mul);
@@ -156,22 +174,18 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t* 
   }
 }
 
-// Epilogue of dQ or dK: the thread (TMEM lane = row, `half` of the epilogue pair) owns columns
-// [i0, i0 + HD/4) and [HD/2 + i0, HD/2 + i0 + HD/4) with i0 = half * HD/4, i.e. both members of
-// every rotate-half pair it stores.  Scaled by `mul`; with a table, rotated by -angle(pos).
-template <int HD>
-__device__ __forceinline__ void store_rot_pairs(uint32_t t_acc, __nv_bfloat16* head_dst, int half,
+// Epilogue of dQ or dK: the thread (TMEM lane = row, part `part` of the QPR threads of the row)
+// owns columns [i0, i0 + Q) and [HD/2 + i0, HD/2 + i0 + Q) with Q = HD / (2 QPR) and
+// i0 = part * Q, i.e. both members of every rotate-half pair it stores.  Scaled by `mul`; with a
+// table, rotated by -angle(pos).
+template <int HD, int QPR>
+__device__ __forceinline__ void store_rot_pairs(uint32_t t_acc, __nv_bfloat16* head_dst, int part,
                                                 float mul, const float* cs, int pos, bool valid) {
-  constexpr int Q4 = HD / 4, H2 = HD / 2;
-  const int i0 = half * Q4;
+  constexpr int Q4 = HD / (2 * QPR), H2 = HD / 2;
+  const int i0 = part * Q4;
   uint32_t a[Q4], b[Q4];
-  if constexpr (Q4 == 32) {
-    CFB_TMEM_LD32(t_acc + i0, a);
-    CFB_TMEM_LD32(t_acc + H2 + i0, b);
-  } else {
-    CFB_TMEM_LD16(t_acc + i0, a);
-    CFB_TMEM_LD16(t_acc + H2 + i0, b);
-  }
+  tmem_ld_n<Q4>(t_acc + i0, a);
+  tmem_ld_n<Q4>(t_acc + H2 + i0, b);
   tmem_ld_wait();
   if (!valid) return;
   uint32_t oa[Q4 / 2], ob[Q4 / 2];
@@ -199,8 +213,10 @@ __device__ __forceinline__ void store_rot_pairs(uint32_t t_acc, __nv_bfloat16* h
   }
 }
 
-template <int HD>
-__global__ void __launch_bounds__(320, 1)
+// NSW softmax / epilogue warps (8 or 16): QPR = NSW / 4 threads share a row of the 64-column
+// score tiles, CPT = 64 / QPR columns each.
+template <int HD, int NSW = 8>
+__global__ void __launch_bounds__(64 + 32 * NSW, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmR,   // qkv_k, box 64 x 128 rows
                        const __grid_constant__ CUtensorMap tmQ,   // qkv_k, box 64 x 64 rows
                        const __grid_constant__ CUtensorMap tmO,   // do_k,  box 64 x 64 rows
@@ -223,15 +239,15 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(smem_u32(&bar->a_full[i]), 1);
       mbar_init(smem_u32(&bar->a_empty[i]), 1);
       mbar_init(smem_u32(&bar->s_full[i]), 1);
-      mbar_init(smem_u32(&bar->s_free[i]), 8);
+      mbar_init(smem_u32(&bar->s_free[i]), NSW);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(&bar->st_full[s]), 1);
       mbar_init(smem_u32(&bar->st_empty[s]), 1);
     }
-    mbar_init(smem_u32(&bar->p_ready), 8);
+    mbar_init(smem_u32(&bar->p_ready), NSW);
     mbar_init(smem_u32(&bar->mm_done), 1);
-    mbar_init(smem_u32(&bar->acc_free), 8);
+    mbar_init(smem_u32(&bar->acc_free), NSW);
     mbar_init(smem_u32(&bar->drain), 1);
     bar->abort = 0;
     fence_mbar_init();
@@ -407,11 +423,14 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue, warps 2-9
+    constexpr int QPR = NSW / 4;     // threads per tile row
+    constexpr int CPT = BC / QPR;    // score columns per thread
     const int quad = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;
     const int r = quad * 32 + lane;  // tile row == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    constexpr int OH = HD / 2;       // output columns per thread in the epilogue
+    constexpr int OH = HD / QPR;     // dV output columns per thread in the epilogue
+    constexpr int OCH = OH < 32 ? OH : 32;
     int k = 0, g = 0;
     bool ok = true;
     for (; ok; ++k) {
@@ -427,11 +446,11 @@ __global__ void __launch_bounds__(320, 1)
         const int kc = j0 + r;  // compact key of this row
         const int qb_first = j0 / BC;
         const int nqb = t.n_it / group;
-        // lse / delta of the 32 queries of a step: lane k holds query i0 + k; loaded one step
-        // ahead so that the global-load latency is off the critical path
+        // lse / delta of the CPT queries of a step: lane k holds query i0 + k % CPT; loaded one
+        // step ahead so that the global-load latency is off the critical path
         auto stat_row = [&](int it) -> long long {
           const int hh = t.head * group + it / nqb;
-          const int q = (qb_first + it % nqb) * BC + half * 32 + lane;
+          const int q = (qb_first + it % nqb) * BC + part * CPT + (lane % CPT);
           return static_cast<long long>(rowk + min(q, p.Sk - 1)) * p.nh + hh;
         };
         float l2_next, dl_next;
@@ -442,7 +461,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         for (int it = 0; it < t.n_it; ++it) {
           const int gg = g + it, sb = gg & 1;
-          const int i0 = (qb_first + it % nqb) * BC + half * 32;  // this thread's first query
+          const int i0 = (qb_first + it % nqb) * BC + part * CPT;  // this thread's first query
           const float l2_lane = l2_next, dl_lane = dl_next;
           if (it + 1 < t.n_it) {
             const long long qr = stat_row(it + 1);
@@ -455,17 +474,17 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          uint32_t s[32], dp[32];
-          CFB_TMEM_LD32(lane_addr + kColS + sb * BC + half * 32, s);
-          CFB_TMEM_LD32(lane_addr + kColDP + sb * BC + half * 32, dp);
+          uint32_t s[CPT], dp[CPT];
+          tmem_ld_n<CPT>(lane_addr + kColS + sb * BC + part * CPT, s);
+          tmem_ld_n<CPT>(lane_addr + kColDP + sb * BC + part * CPT, dp);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&bar->s_free[sb]));
           const int lo = kc - i0, hi = p.Sk - i0;  // query column c is visible iff lo <= c < hi
-          uint32_t pp[16], pd[16];
+          uint32_t pp[CPT / 2], pd[CPT / 2];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < CPT / 2; ++i) {
             float pv[2], dv[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
@@ -487,8 +506,8 @@ __global__ void __launch_bounds__(320, 1)
             ok = false;
             break;
           }
-          write_row_half(sbase + L::OFF_P, r, half, pp);
-          write_row_half(sbase + L::OFF_DS, r, half, pd);
+          write_row_part<CPT>(sbase + L::OFF_P, r, part, pp);
+          write_row_part<CPT>(sbase + L::OFF_DS, r, part, pd);
           fence_async_shared();
           tc_fence_before();
           __syncwarp();
@@ -502,14 +521,14 @@ __global__ void __launch_bounds__(320, 1)
         const bool kvalid = kc < p.Sk;
         const long long krow = static_cast<long long>(rowk + min(kc, p.Sk - 1));
         __nv_bfloat16* drow = p.dqkv + krow * p.ld;
-        store_rot_pairs<HD>(lane_addr + kColAcc, drow + kcol, half, p.scale, p.cs,
-                            kvalid ? __ldg(p.pos_k + krow) : 0, kvalid);
+        store_rot_pairs<HD, QPR>(lane_addr + kColAcc, drow + kcol, part, p.scale, p.cs,
+                                 kvalid ? __ldg(p.pos_k + krow) : 0, kvalid);
 #pragma unroll
-        for (int cc = 0; cc < OH / 32; ++cc) {
-          uint32_t dv[32];
-          CFB_TMEM_LD32(lane_addr + kColAcc + HD + half * OH + cc * 32, dv);
+        for (int cc = 0; cc < OH / OCH; ++cc) {
+          uint32_t dv[OCH];
+          tmem_ld_n<OCH>(lane_addr + kColAcc + HD + part * OH + cc * OCH, dv);
           tmem_ld_wait();
-          if (kvalid) store_row32(drow + vcol + half * OH + cc * 32, dv, 1.f);
+          if (kvalid) store_row_n<OCH>(drow + vcol + part * OH + cc * OCH, dv, 1.f);
         }
       } else {
         const int qc = t.blk * BR + r;  // compact query of this row
@@ -526,17 +545,17 @@ __global__ void __launch_bounds__(320, 1)
             break;
           }
           tc_fence_after();
-          uint32_t s[32], dp[32];
-          CFB_TMEM_LD32(lane_addr + kColS + sb * BC + half * 32, s);
-          CFB_TMEM_LD32(lane_addr + kColDP + sb * BC + half * 32, dp);
+          uint32_t s[CPT], dp[CPT];
+          tmem_ld_n<CPT>(lane_addr + kColS + sb * BC + part * CPT, s);
+          tmem_ld_n<CPT>(lane_addr + kColDP + sb * BC + part * CPT, dp);
           tmem_ld_wait();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&bar->s_free[sb]));
-          const int lim = min(qpos, p.S - 1) - (j * BC + half * 32);  // key column c visible iff c <= lim
-          uint32_t pd[16];
+          const int lim = min(qpos, p.S - 1) - (j * BC + part * CPT);  // key column c visible iff c <= lim
+          uint32_t pd[CPT / 2];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
+          for (int i = 0; i < CPT / 2; ++i) {
             float dv[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
@@ -552,7 +571,7 @@ __global__ void __launch_bounds__(320, 1)
             ok = false;
             break;
           }
-          write_row_half(sbase + L::OFF_DS, r, half, pd);
+          write_row_part<CPT>(sbase + L::OFF_DS, r, part, pd);
           fence_async_shared();
           tc_fence_before();
           __syncwarp();
@@ -562,8 +581,8 @@ __global__ void __launch_bounds__(320, 1)
         const int gl = g + t.n_it - 1;
         if (!mbar_wait(smem_u32(&bar->mm_done), gl & 1, abort_flag, p.err, kErrWaitSoftmax)) break;
         tc_fence_after();
-        store_rot_pairs<HD>(lane_addr + kColAcc, p.dqkv + qr * p.ld + t.head * HD, half, p.scale,
-                            p.cs, qpos, qvalid);
+        store_rot_pairs<HD, QPR>(lane_addr + kColAcc, p.dqkv + qr * p.ld + t.head * HD, part,
+                                 p.scale, p.cs, qpos, qvalid);
       }
       // accumulators read: the next item's first accumulate may overwrite them
       tc_fence_before();
@@ -639,15 +658,25 @@ int cfb_attn_bwd_tc(const void* qkv_k, long long ld_qkv, const void* qkv_full, c
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
   }
   const int grid = p.n_items < n_sm ? p.n_items : n_sm;
-  auto go = [&](auto kern, int bytes, bool& configured) -> int {
+  auto go = [&](auto kern, int bytes, int threads, bool& configured) -> int {
     if (!configured) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
       configured = true;
     }
-    kern<<<grid, 320, bytes, st>>>(tR, tQ, tO, tOk, tF, p);
+    kern<<<grid, threads, bytes, st>>>(tR, tQ, tO, tOk, tF, p);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
   };
-  static bool configured64 = false, configured128 = false;
-  if (hd == 64) return go(attn_bwd_tc_kernel<64>, Cfg<64>::BYTES, configured64);
-  return go(attn_bwd_tc_kernel<128>, Cfg<128>::BYTES, configured128);
+  // CFB_ATTN_BWD_WARPS: softmax / epilogue warps per CTA, 8 (default) or 16.  16 measured
+  // slower (TinyLlama layer, keep 0.5: 0.528 vs 0.499 ms; hd 128: 1.564 vs 1.526 ms).
+  static const int nsw = [] {
+    const char* e = std::getenv("CFB_ATTN_BWD_WARPS");
+    return (e && std::atoi(e) == 16) ? 16 : 8;
+  }();
+  static bool cfg[4] = {false, false, false, false};
+  if (nsw == 16) {
+    if (hd == 64) return go(attn_bwd_tc_kernel<64, 16>, Cfg<64>::BYTES, 576, cfg[0]);
+    return go(attn_bwd_tc_kernel<128, 16>, Cfg<128>::BYTES, 576, cfg[1]);
+  }
+  if (hd == 64) return go(attn_bwd_tc_kernel<64, 8>, Cfg<64>::BYTES, 320, cfg[2]);
+  return go(attn_bwd_tc_kernel<128, 8>, Cfg<128>::BYTES, 320, cfg[3]);
 }

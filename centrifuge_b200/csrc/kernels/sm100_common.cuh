@@ -286,6 +286,12 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
         "=r"(r[13]), "=r"(r[14]), "=r"(r[15])                                                  \
       : "r"(taddr))
 
+#define CFB_TMEM_LD8(taddr, r)                                                                  \
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"        \
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),       \
+                 "=r"(r[6]), "=r"(r[7])                                                        \
+               : "r"(taddr))
+
 #define CFB_TMEM_ST32(taddr, r)                                                                 \
   asm volatile(                                                                                 \
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"  \
