@@ -121,9 +121,23 @@ class TPLlamaCore(torch.nn.Module):
 
     def reduce_replicated_grads(self) -> None:
         """Sum the gradients of replicated weights (embedding, RMSNorm) over the TP group.
-        Call once per optimizer step, on the gradients accumulated over the micro-batches."""
-        for name in self.replicated:
-            self.tp.all_reduce_(self.flat.grads[name])
+        Call once per optimizer step, on the gradients accumulated over the micro-batches.
+        The small ones (the RMSNorm weights of every layer) travel packed in one all-reduce
+        instead of one collective each; large ones are reduced in place."""
+        if self.tp.size == 1:
+            return
+        small = [self.flat.grads[n] for n in self.replicated
+                 if self.flat.grads[n].numel() <= (1 << 22)]
+        for n in self.replicated:
+            if self.flat.grads[n].numel() > (1 << 22):
+                self.tp.all_reduce_(self.flat.grads[n])
+        if small:
+            packed = torch.cat([g.reshape(-1) for g in small])
+            self.tp.all_reduce_(packed)
+            off = 0
+            for g in small:
+                g.copy_(packed[off:off + g.numel()].view_as(g))
+                off += g.numel()
 
     def replicated_ranges(self):
         return [self.flat.range_of(n) for n in self.replicated]
