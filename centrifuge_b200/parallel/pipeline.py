@@ -12,11 +12,13 @@ Per micro-batch the last stage computes the per-token loss, the selection mask a
 backward.  The mask is sent back with the gradient, so earlier stages build the same kept-row
 layout; backward point-to-point messages carry only the (padded) kept rows ``[C, H]`` of the
 sequence shard, forward messages the full shard ``[T/TP, H]``.  Sends are non-blocking
-(NCCL / gloo ``isend``); receives of a known shape are posted one schedule slot ahead of their
-use (a forward's input, a backward's mask) so that the transfer overlaps the slot before.
+(NCCL / gloo ``isend``); receives are posted at their use.  ``prefetch`` posts the receives of
+a known shape (a forward's input, a backward's mask) one schedule slot ahead instead; measured
+slower on B200 (the waiting receive kernels hold SMs), so it is off by default.
 """
 from __future__ import annotations
 
+import os
 from collections import deque
 from dataclasses import dataclass
 from typing import List, Optional
@@ -118,6 +120,11 @@ class PipelineTrainer:
         # (after its receive, before its send), read by busy_ms() to measure the bubble
         self.timing = False
         self._events: List = []
+        # prefetch=True (CFB_PP_PREFETCH=1): post the receives of known shape one slot ahead.
+        # Off by default: an early receive holds its NCCL kernel on an SM while it waits, which
+        # stalls the stage's compute (TP2 x PP2, 16 Llama-3-8B layers, 8 micro-batches: 603 vs
+        # 376 ms / step with fused TP collectives, 425 vs 373 ms with NCCL ones).
+        self.prefetch = os.environ.get("CFB_PP_PREFETCH", "0") == "1"
         # device errors (bounded waits that ran out, bad masks) surface one step late
         self.status = None
         if check_device_errors and torch.device(self.device).type == "cuda":
@@ -180,14 +187,14 @@ class PipelineTrainer:
         hidden = None
         if not self.first:
             hidden = self._take(("f", i), self._fwd_shape(batches[i]), dt, self.g.prev)
-            if i + 1 < len(batches):
+            if self.prefetch and i + 1 < len(batches):
                 self._post(("f", i + 1), self._fwd_shape(batches[i + 1]), dt, self.g.prev)
         t0 = self._mark()
         out = self.core(input_ids=ids, hidden=hidden, batch_shape=(B, S))
         if not self.last:
             self._mark(t0)
             self._isend(out.hidden.detach(), self.g.next)
-            if prefetch_bwd >= 0:
+            if self.prefetch and prefetch_bwd >= 0:
                 pb, ps = batches[prefetch_bwd][0].shape
                 self._post(("m", prefetch_bwd), (pb, ps), torch.long, self.g.next)
             return {"i": i, "ids": ids, "out": out, "B": B, "S": S}
