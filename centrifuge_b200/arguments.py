@@ -88,6 +88,9 @@ def build_parser() -> argparse.ArgumentParser:
     g.add_argument("--num_microbatches", type=int, default=None,
                    help="pipeline micro-batches per step (default: gradient accumulation)")
     g.add_argument("--grad_reducer", type=str, default="auto", choices=["auto", "nccl", "symm"])
+    g.add_argument("--grad_mode", type=str, default="ring", choices=["ring", "full"],
+                   help="ZeRO-2 gradients: ring = partitioned (bucket slots reduce-scattered "
+                        "every micro-batch), full = full local buffer reduced once per step")
     g.add_argument("--max_steps", type=int, default=None)
     g.add_argument("--log_file", type=str, default=None, help="JSONL metrics file")
     g.add_argument("--synthetic_data", action="store_true", default=False,

@@ -84,13 +84,15 @@ class NativeRunner:
         if world > 1 and args.grad_reducer in ("auto", "symm") and device.type == "cuda":
             try:
                 from .parallel.symm import SymmReducer
-                reducer = SymmReducer.create(self.model.flat, group)
+                reducer = SymmReducer.create(self.model.flat, group,
+                                             ring=args.grad_mode == "ring" and args.zero_stage == 2)
             except Exception:
                 if args.grad_reducer == "symm":
                     raise
         self.opt = ZeroAdamW(self.model.flat, group=group, stage=args.zero_stage,
                              lr=args.learning_rate, betas=(0.9, 0.95), eps=1e-8,
-                             weight_decay=args.weight_decay, grad_clip=1.0, reducer=reducer)
+                             weight_decay=args.weight_decay, grad_clip=1.0, reducer=reducer,
+                             grad_mode=args.grad_mode if args.zero_stage == 2 else "full")
         drop = args.drop_rate if args.dropping_strategy not in ("none", None) else 0.0
         self.trainer = Trainer(self.model, self.opt, drop_rate=drop,
                                strategy=args.dropping_strategy, grad_accum=args.gradient_accumulation_steps,

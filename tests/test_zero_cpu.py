@@ -102,3 +102,17 @@ def test_ring_gradient_memory_at_tinyllama_scale(world):
     full = flat.numel * 4
     # TinyLlama: 24 buckets of <= 65.5M elements, 4 slots = 1.05 GB against 4.4 GB
     assert ring < 0.25 * full and ring + shard < full, (ring, shard, full)
+
+
+@pytest.mark.parametrize("mode", ["ring", "full"])
+def test_data_parallel_training_is_deterministic(mode, tmp_path):
+    """Distributed determinism: two identical 2-rank ZeRO-2 runs give bit-identical parameters,
+    and after every step's parameter all-gather all ranks hold the same bits."""
+    world, ga, steps = 2, 2, 2
+    a = run_ranks(_train, world, 2, ga, steps, str(tmp_path / "a"), False, mode)
+    b = run_ranks(_train, world, 2, ga, steps, str(tmp_path / "b"), False, mode)
+    for name in a[0][0]:
+        for r in range(world):
+            assert (a[r][0][name] == b[r][0][name]).all(), (mode, r, name)
+        assert (a[0][0][name] == a[1][0][name]).all(), (mode, name)
+    assert a[0][1] == b[0][1]
