@@ -80,3 +80,33 @@ def test_tp2_matches_single(drop, tmp_path):
             gp = torch.from_numpy(gp)
             err = ((gp - want_p[name]).norm() / (want_p[name].norm() + 1e-12)).item()
             assert err < 1e-4, (p, name, err)
+
+
+class _FakeTP:
+    def __init__(self, size, rank):
+        self.size, self.rank = size, rank
+
+
+def test_kept_layout_index_maps():
+    """Padded kept-row layout of the filtered TP backward: per-rank counts, the compact <->
+    padded maps and the shard-local rows, for several ranks and for one shard (no host read)."""
+    from centrifuge_b200.parallel.tensor_parallel import KeptLayout
+    T = 32
+    rows = torch.tensor([0, 3, 4, 9, 17, 18, 19, 30], dtype=torch.int32)
+    P = 4
+    lays = [KeptLayout(rows, T, _FakeTP(P, p), "cpu") for p in range(P)]
+    assert lays[0].counts == [3, 1, 3, 1] and all(l.C == 3 for l in lays)
+    # every compact row lands in its owner's padded slot and maps back
+    for l in lays:
+        padded = torch.arange(P * l.C)
+        assert torch.equal(l.p2c[l.c2p.long()].long(), torch.arange(rows.numel()))
+        assert (l.p2c[(padded % l.C) >= torch.tensor(l.counts).repeat_interleave(l.C)] ==
+                rows.numel()).all()
+    shard = T // P
+    for p, l in enumerate(lays):
+        mine = rows[(rows // shard) == p] - p * shard
+        assert torch.equal(l.local[:l.count], mine)
+    one = KeptLayout(rows, T, _FakeTP(1, 0), "cpu")
+    assert one.C == one.Tk == one.count == rows.numel() and one.counts == [rows.numel()]
+    assert torch.equal(one.local, rows) and torch.equal(one.c2p, torch.arange(8, dtype=torch.int32))
+    assert torch.equal(one.p2c, one.c2p) and not one.identity
